@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""Benchmark of the FG-CPAB hot path on B200: fwd+grad warped points/s.
+
+Workload: Cpab([20, 20], zero_boundary=True),
+batch 16, theta ~ N(0, 1), 125,000 points ~ U[0,1]^2 per GPU, nstepsolver 50;
+one step = transform_grid forward + MSE(x_t, x) + backward to theta, through
+the public API.  With N GPUs (torchrun, one process per GPU) every rank
+integrates its own 125,000 points (weak scaling) and the gradient is summed
+with one NCCL allreduce of dtheta per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  `value` is the device-resident throughput
+(CUDA events around every step, L2 flushed between steps, max over ranks);
+`e2e` is the same step with pinned-host inputs copied in and the loss and
+gradient copied out inside the timed region.  `--impl reference` times the
+CPU restatement of the reference kernels (oracle/, all host threads) on a
+bounded sample of the same workload.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "fg-cpab_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+TESS = [20, 20]
+BATCH = 16
+N_POINTS = 125_000
+NSTEP = 50
+METRIC = "fwd+grad warped points/sec"
+UNIT = "points/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def config(world):
+    return {
+        "workload": "2D Cpab([20,20], zero_boundary=True): batch 16, 125,000 U[0,1]^2 points per "
+                    "GPU, theta~N(0,1), nstepsolver 50; transform_grid + MSE(x_t, x) + backward "
+                    "to theta",
+        "tess": TESS, "batch": BATCH, "points_per_gpu": N_POINTS, "nstepsolver": NSTEP,
+        "global_batch": BATCH * N_POINTS * world,
+        "parallelism": "points sharded over %d GPU(s), dtheta allreduce" % world,
+        "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20),
+    }
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except Exception:
+                pass
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def max_over_ranks(x, world):
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the oracle restatement of the reference kernels.
+# ---------------------------------------------------------------------------
+
+def cpu_step(O, basis, pts, theta):
+    """One fwd+grad of the reference composition on CPU; returns dtheta."""
+    x, As, _ = O.transform(TESS, basis, pts, theta, NSTEP)
+    gout = (2.0 / x.size) * (x - pts[None])
+    mom, _ = O.adjoint(TESS, pts, As, gout.astype(np.float32), NSTEP, False, want_points=False)
+    return O.project(basis, mom)
+
+
+def cpu_sample_points(O, basis, theta, target_s):
+    """Points per sample so that one sample takes about target_s seconds."""
+    probe = 2048
+    pts = np.random.default_rng(1).random((2, probe), dtype=np.float32)
+    t0 = time.perf_counter()
+    cpu_step(O, basis, pts, theta)
+    dt = time.perf_counter() - t0
+    n = int(probe * target_s / max(dt, 1e-6))
+    return max(1024, min(N_POINTS, n))
+
+
+def cpu_baseline(basis, theta_np, target_s=10.0):
+    from oracle import oracle as O
+    n = cpu_sample_points(O, basis, theta_np, target_s)
+    pts = np.random.default_rng(1).random((2, n), dtype=np.float32)
+    t0 = time.perf_counter()
+    cpu_step(O, basis, pts, theta_np)
+    dt = time.perf_counter() - t0
+    return {"value": n * BATCH / dt, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": "%d of the %d points x batch %d, one fwd+grad (A-build, expm, integrate, "
+                      "adjoint, projection), %.1f s" % (n, N_POINTS, BATCH, dt)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from cpab import Cpab
+    from oracle import oracle as O
+    C = Cpab(TESS, zero_boundary=True)
+    theta = torch.randn(BATCH, C.params.d, generator=torch.Generator().manual_seed(0)).numpy()
+    n = cpu_sample_points(O, C.params.basis, theta, 3.0)
+    pts = np.random.default_rng(1).random((2, n), dtype=np.float32)
+    for _ in range(args.warmup):
+        cpu_step(O, C.params.basis, pts, theta)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(O, C.params.basis, pts, theta)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = n * BATCH / dt
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config(1), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+                         "sample": "%d of %d points x batch %d per step" % (n, N_POINTS, BATCH)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm.
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local):
+    from cpab import Cpab, _native
+    from cpab.distributed import transform_grid_sharded
+
+    dev = torch.device("cuda", local)
+    C = Cpab(TESS, zero_boundary=True)
+    d = C.params.d
+    theta_h = torch.randn(BATCH, d, generator=torch.Generator().manual_seed(0))
+    pts_h = torch.rand(2, N_POINTS, generator=torch.Generator().manual_seed(1 + rank))
+    group = dist.group.WORLD if world > 1 else None
+
+    def fwd_grad(pts, theta):
+        t = theta.detach().requires_grad_(True)
+        if group is None:
+            out = C.transform_grid(pts, t)
+        else:
+            out = transform_grid_sharded(C, pts, t, group)
+        loss = ((out - pts) ** 2).mean()
+        loss.backward()
+        return loss, t.grad
+
+    # Per-launch timing of the integration kernels, on the stream they run on.
+    timings = {"forward": [], "backward": []}
+    orig = {"forward": _native.forward, "backward": _native.backward}
+
+    def timed(name):
+        def call(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = orig[name](*a, **k)
+            e.record()
+            if timings.get("on"):
+                timings[name].append((s, e))
+            return r
+        return call
+
+    _native.forward, _native.backward = timed("forward"), timed("backward")
+
+    pts = pts_h.to(dev)
+    theta = theta_h.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    for _ in range(args.warmup):
+        fwd_grad(pts, theta)
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    if rank == 0:
+        clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    timings["on"] = True
+    ev = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fwd_grad(pts, theta)
+        e.record()
+        ev.append((s, e))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    timings["on"] = False
+    clk = clocks.stop() if rank == 0 else None
+    total_ms = sum(s.elapsed_time(e) for s, e in ev)
+    kern = {k: sum(s.elapsed_time(e) for s, e in v) / max(len(v), 1) for k, v in timings.items()
+            if k != "on"}
+    total_ms = max_over_ranks(total_ms, world)
+    kern = {k: max_over_ranks(v, world) for k, v in kern.items()}
+    ms_step = total_ms / args.steps
+    pairs_step = BATCH * N_POINTS * world
+    value = pairs_step / (ms_step * 1e-3)
+
+    # End to end: pinned host inputs in, loss and gradient out, every step.
+    pts_pin = pts_h.pin_memory()
+    th_pin = theta_h.pin_memory()
+    loss_pin = torch.empty(1, pin_memory=True)
+    grad_pin = torch.empty(BATCH, d, pin_memory=True)
+    pts_d = torch.empty_like(pts)
+    th_d = torch.empty_like(theta)
+
+    def e2e_step():
+        pts_d.copy_(pts_pin, non_blocking=True)
+        th_d.copy_(th_pin, non_blocking=True)
+        loss, grad = fwd_grad(pts_d, th_d)
+        loss_pin.copy_(loss.detach().reshape(1), non_blocking=True)
+        grad_pin.copy_(grad, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        e2e_step()
+        e.record()
+        ev.append((s, e))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world) / args.steps
+    h2d = pts_h.numel() * 4 + theta_h.numel() * 4
+    d2h = 4 + theta_h.numel() * 4
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        nC = C.params.nC
+        # Algorithmic bytes of one backward launch: points (shared by the
+        # batch), upstream gradient, cell matrices in, moments out.
+        bwd_bytes = (2 * N_POINTS + BATCH * 2 * N_POINTS + 2 * BATCH * nC * 6) * 4
+        ach = bwd_bytes / (kern["backward"] * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config(world),
+            "e2e": {"value": pairs_step / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "kernel": "k_backward (fused adjoint)",
+                         "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": bwd_bytes},
+            "kernel_ms": kern,
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(C.params.basis, theta_h.numpy())
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = init_dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

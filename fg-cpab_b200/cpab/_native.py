@@ -1,0 +1,210 @@
+"""ctypes binding of libcpab_b200.so (the C ABI in include/cpab_b200.h).
+
+Tensors cross the boundary as raw device pointers plus sizes; every call is
+enqueued on torch's current stream of the tensors' device.  There is no CPU
+fallback: if the library is missing or the tensors are not CUDA tensors the
+call raises.
+"""
+import ctypes
+import os
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcpab_b200.so")
+
+_c_int, _c_i64, _c_float, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+# name -> argtypes (all return int status)
+_SIGNATURES = {
+    "cpab_b200_expm": [_c_int, _p, _c_i64, _c_float, _p, _p],
+    "cpab_b200_build_A": [_c_int, _c_i64, _c_i64, _c_int, _p, _p, _p, _p, _c_float, _p, _p, _p],
+    "cpab_b200_forward": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _c_int, _c_int, _p, _p],
+    "cpab_b200_forward_1d_closed_form": [_p, _c_i64, _c_int, _p, _c_int, _c_int, _p, _p],
+    "cpab_b200_backward": [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _p, _c_int, _c_int, _p, _p,
+                           _p],
+    "cpab_b200_cell_index": [_c_int, _p, _p, _c_i64, _p, _p],
+    "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
+    "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],
+    "cpab_b200_interpolate_backward": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p, _p, _p],
+}
+
+EXPORTS = tuple(_SIGNATURES) + ("cpab_b200_version", "cpab_b200_max_steps",
+                                "cpab_b200_last_error")
+
+_lib = None
+
+
+class CpabNativeError(RuntimeError):
+    """A libcpab_b200 call returned a non-zero status."""
+
+
+def lib():
+    """Load (once) and return the native library."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                "libcpab_b200.so is not built (expected at %s); run "
+                "`python fg-cpab_b200/build.py` first" % LIB_PATH)
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        L.cpab_b200_version.restype = ctypes.c_int
+        L.cpab_b200_max_steps.restype = ctypes.c_int
+        L.cpab_b200_last_error.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def max_steps():
+    return lib().cpab_b200_max_steps()
+
+
+def _check(status):
+    if status != 0:
+        msg = lib().cpab_b200_last_error().decode(errors="replace")
+        raise CpabNativeError(msg or "libcpab_b200 error %d" % status)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require(t, name, dtype=torch.float32):
+    if not t.is_cuda:
+        raise RuntimeError("%s must be a CUDA tensor (no CPU path)" % name)
+    if t.dtype != dtype:
+        raise TypeError("%s must be %s, got %s" % (name, dtype, t.dtype))
+    if not t.is_contiguous():
+        raise RuntimeError("%s must be contiguous" % name)
+
+
+def _i32_array(values):
+    return (ctypes.c_int32 * len(values))(*[int(v) for v in values])
+
+
+def _i64_array(values):
+    return (ctypes.c_int64 * len(values))(*[int(v) for v in values])
+
+
+# ---------------------------------------------------------------------------
+# Thin wrappers: shapes in, tensors out (allocated with torch on the device).
+# ---------------------------------------------------------------------------
+
+def expm(As, dT):
+    """Trels = expm(dT * A) for As [n, ndim, ndim+1]."""
+    _require(As, "As")
+    n, nd = As.shape[0], As.shape[1]
+    out = torch.empty_like(As)
+    with torch.cuda.device(As.device):
+        _check(lib().cpab_b200_expm(nd, _ptr(As), n, float(dT), _ptr(out), _stream(As.device)))
+    return out
+
+
+def build_A(ndim, nC, basis, theta, dT=None):
+    """As = reshape(B theta^T) [n_theta, nC, ndim, ndim+1] and, when dT is given,
+    Trels = expm(dT * As).  ``basis`` is a DeviceBasis."""
+    _require(theta, "theta")
+    n_theta = theta.shape[0]
+    As = torch.empty((n_theta, nC, ndim, ndim + 1), device=theta.device, dtype=torch.float32)
+    trels = torch.empty_like(As) if dT is not None else None
+    with torch.cuda.device(theta.device):
+        _check(lib().cpab_b200_build_A(
+            ndim, nC, basis.d, n_theta, _ptr(basis.rowptr), _ptr(basis.colidx), _ptr(basis.vals),
+            _ptr(theta), float(dT) if dT is not None else 0.0, _ptr(As), _ptr(trels),
+            _stream(theta.device)))
+    return As, trels
+
+
+def forward(ndim, nc, points, batched, trels, As, nstepsolver, adaptive):
+    _require(points, "points")
+    _require(As, "As")
+    n_theta = As.shape[0]
+    nP = points.shape[-1]
+    out = torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
+    with torch.cuda.device(As.device):
+        if ndim == 1:
+            _check(lib().cpab_b200_forward_1d_closed_form(
+                _ptr(points), nP, int(batched), _ptr(As), n_theta, int(nc[0]), _ptr(out),
+                _stream(As.device)))
+        else:
+            _require(trels, "Trels")
+            _check(lib().cpab_b200_forward(
+                ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(trels), _ptr(As),
+                n_theta, int(nstepsolver), int(adaptive), _ptr(out), _stream(As.device)))
+    return out
+
+
+def backward(ndim, nc, points, batched, As, grad_out, nstepsolver, adaptive, want_points):
+    """Returns (moments [n_theta, nC, ppc], grad_points [n_theta, ndim, nP] or None)."""
+    _require(points, "points")
+    _require(As, "As")
+    _require(grad_out, "grad")
+    n_theta, nC = As.shape[0], As.shape[1]
+    nP = points.shape[-1]
+    ppc = ndim * (ndim + 1)
+    moments = torch.empty((n_theta, nC, ppc), device=As.device, dtype=torch.float32)
+    gp = (torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
+          if want_points else None)
+    with torch.cuda.device(As.device):
+        _check(lib().cpab_b200_backward(
+            ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(As), n_theta,
+            _ptr(grad_out), int(nstepsolver), int(adaptive), _ptr(moments), _ptr(gp),
+            _stream(As.device)))
+    return moments, gp
+
+
+def cell_index(nc, points):
+    """Cell of every point, points [ndim, n] -> int32 [n]."""
+    _require(points, "points")
+    nd, n = points.shape
+    out = torch.empty(n, device=points.device, dtype=torch.int32)
+    with torch.cuda.device(points.device):
+        _check(lib().cpab_b200_cell_index(nd, _i32_array(nc), _ptr(points), n, _ptr(out),
+                                          _stream(points.device)))
+    return out
+
+
+def project(basis, moments):
+    """dtheta [n_theta, d] = B^T vec(moments)."""
+    _require(moments, "moments")
+    n_theta = moments.shape[0]
+    D = moments[0].numel()
+    out = torch.empty((n_theta, basis.d), device=moments.device, dtype=torch.float32)
+    with torch.cuda.device(moments.device):
+        _check(lib().cpab_b200_project(
+            basis.d, D, n_theta, _ptr(basis.t_rowptr), _ptr(basis.t_colidx), _ptr(basis.t_vals),
+            _ptr(moments), _ptr(out), _stream(moments.device)))
+    return out
+
+
+def interpolate(ndim, data, grid, outsize):
+    _require(data, "data")
+    _require(grid, "grid")
+    B, C = data.shape[0], data.shape[1]
+    out = torch.empty((B, C, *outsize), device=data.device, dtype=torch.float32)
+    with torch.cuda.device(data.device):
+        _check(lib().cpab_b200_interpolate(
+            ndim, _ptr(data), B, C, _i64_array(data.shape[2:]), _ptr(grid), _i64_array(outsize),
+            _ptr(out), _stream(data.device)))
+    return out
+
+
+def interpolate_backward(ndim, data, grid, outsize, grad_out, want_grid, want_data):
+    _require(data, "data")
+    _require(grid, "grid")
+    _require(grad_out, "grad")
+    B, C = data.shape[0], data.shape[1]
+    gg = torch.empty_like(grid) if want_grid else None
+    gd = torch.empty_like(data) if want_data else None
+    with torch.cuda.device(data.device):
+        _check(lib().cpab_b200_interpolate_backward(
+            ndim, _ptr(data), B, C, _i64_array(data.shape[2:]), _ptr(grid), _i64_array(outsize),
+            _ptr(grad_out), _ptr(gg), _ptr(gd), _stream(data.device)))
+    return gg, gd

@@ -1,0 +1,137 @@
+"""Differentiable CPA transformation of points (cpab/pytorch/transformer.py of
+the reference), backed by libcpab_b200.
+
+Forward:  A = B theta (+ Trels = expm(A / nstepsolver), fused), then the
+          integration kernel (closed form in 1D, nstepsolver exact per-cell
+          steps in 2D/3D).
+Backward: the fused adjoint kernel produces per-cell moments (and the point
+          gradient lambda(0) when the points need one), then one sparse
+          projection dtheta = B^T vec(moments).  Optionally the projected
+          gradient is summed over a process group (points sharded over GPUs).
+"""
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import _native
+
+
+@dataclass
+class DeviceBasis:
+    """CSR copies of B (D x d) and B^T (d x D) on one device, fp32 values."""
+    d: int
+    D: int
+    rowptr: torch.Tensor
+    colidx: torch.Tensor
+    vals: torch.Tensor
+    t_rowptr: torch.Tensor
+    t_colidx: torch.Tensor
+    t_vals: torch.Tensor
+
+
+def _csr_arrays(M, device):
+    M = M.tocsr()
+    M.sort_indices()
+    return (torch.from_numpy(M.indptr.astype(np.int32)).to(device),
+            torch.from_numpy(M.indices.astype(np.int32)).to(device),
+            torch.from_numpy(M.data.astype(np.float32)).to(device))
+
+
+def device_basis(params, device):
+    """B and B^T of ``params.basis`` on ``device``, built once per device.
+
+    (The reference caches its sparse basis for cuda:0 only and rebuilds it
+    from scipy on every call for other devices, cpab/pytorch/transformer.py:47-66.)
+    """
+    cache = params.__dict__.setdefault("_device_basis", {})
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    hit = cache.get(key)
+    if hit is None:
+        B = params.basis
+        r, c, v = _csr_arrays(B, device)
+        tr, tc, tv = _csr_arrays(B.T, device)
+        hit = DeviceBasis(int(B.shape[1]), int(B.shape[0]), r, c, v, tr, tc, tv)
+        cache[key] = hit
+    return hit
+
+
+def CPAB_transformer(points, theta, params, compute_points_grad=False):
+    """Transform points through the CPA velocity field given by theta.
+
+    Arguments:
+        points: [ndim, n_points] or [n_batch, ndim, n_points] CUDA tensor
+        theta: [n_batch, d] CUDA tensor of transformation parameters
+        params: parameter object from Cpab
+        compute_points_grad: bool, return a gradient for the points in backward
+
+    Returns:
+        transformed_points: [n_batch, ndim, n_points]
+    """
+    assert points.is_cuda and theta.is_cuda, "Only GPU tensors supported"
+    assert params.ndim in (1, 2, 3), "GPU transformer supports 1D, 2D, and 3D"
+    assert type(compute_points_grad) == bool, "compute_points_grad must be bool"
+    return _CPABFunction.apply(points, theta, params, compute_points_grad, None)
+
+
+def _layout(points, theta, params):
+    """Validate shapes; returns (batched, nP)."""
+    nd = params.ndim
+    n_theta = theta.shape[0]
+    if theta.dim() != 2 or theta.shape[1] != params.d:
+        raise ValueError("theta must be [n_batch, %d], got %s" % (params.d, tuple(theta.shape)))
+    if points.dim() == 2:
+        if points.shape[0] != nd:
+            raise ValueError("points must be [%d, n_points], got %s" % (nd, tuple(points.shape)))
+        return False, points.shape[1]
+    if points.dim() == 3 and points.shape[0] == n_theta and points.shape[1] == nd:
+        return True, points.shape[2]
+    raise ValueError("points must be [%d, n_points] or [%d, %d, n_points], got %s"
+                     % (nd, n_theta, nd, tuple(points.shape)))
+
+
+def _nc(params):
+    return [int(c) for c in params.nc]
+
+
+class _CPABFunction(torch.autograd.Function):
+    """A = B theta -> integrate; backward: fused adjoint moments -> B^T projection."""
+
+    @staticmethod
+    def forward(ctx, points, theta, params, compute_points_grad=False, group=None):
+        batched, _ = _layout(points, theta, params)
+        nd = params.ndim
+        basis = device_basis(params, theta.device)
+        theta_c = theta.contiguous()
+        points_c = points.contiguous()
+        T = int(params.nstepsolver)
+        adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
+        dT = None if nd == 1 else 1.0 / T
+        As, trels = _native.build_A(nd, int(params.nC), basis, theta_c, dT)
+        out = _native.forward(nd, _nc(params), points_c, batched, trels, As, T, adaptive)
+        ctx.params = params
+        ctx.batched = batched
+        ctx.nstepsolver = T
+        ctx.adaptive = adaptive
+        ctx.compute_points_grad = compute_points_grad
+        ctx.group = group
+        ctx.save_for_backward(points_c, As)
+        return out
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad):
+        points, As = ctx.saved_tensors
+        params = ctx.params
+        want_points = ctx.compute_points_grad and ctx.needs_input_grad[0]
+        moments, grad_points = _native.backward(
+            params.ndim, _nc(params), points, ctx.batched, As, grad.contiguous(),
+            ctx.nstepsolver, ctx.adaptive, want_points)
+        if grad_points is not None and points.dim() == 2:
+            grad_points = grad_points.sum(dim=0)
+        grad_theta = None
+        if ctx.needs_input_grad[1]:
+            grad_theta = _native.project(device_basis(params, As.device), moments)
+            if ctx.group is not None:
+                torch.distributed.all_reduce(grad_theta, group=ctx.group)
+        return grad_points, grad_theta, None, None, None

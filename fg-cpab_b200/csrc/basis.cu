@@ -1,0 +1,298 @@
+// Parameter-space kernels: A = B theta (fused with the per-cell matrix
+// exponential Trels = expm(dT A)), the stand-alone expm, and the projection
+// dtheta = B^T vec(M).
+//
+// These are small sparse contractions (a handful of nonzeros per row for
+// zero-boundary bases) -- gathers, not GEMMs -- so they run on the SIMT
+// pipes: one thread per (transformation, cell) for the A-build, one thread
+// per (transformation, basis column) for the projection with the
+// transformation index fastest so that CSR index/value loads are broadcast.
+#include <cuda_runtime.h>
+
+#include "launch.h"
+
+namespace cpab {
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// Matrix exponential of the affine matrix dT*[A; 0 .. 0] (top rows only).
+// Scaling and squaring with the (2,2) Pade approximant
+//   R = (I - M/2 + M^2/12)^-1 (I + M/2 + M^2/12),
+// the scheme of cpab/core/cpab_ops_2d.cu:585-701 (2D) and
+// cpab/core/cpab_ops_3d.cu:538-674 (3D); the 1D case is the closed form of
+// cpab/core/cpab_ops_1d.cu:442-467.  The operation order follows those
+// kernels so Trels agree to the last bits.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int squarings(float norm) {
+  return norm > 0.5f ? (int)ceilf(log2f(norm * 2.0f)) : 0;
+}
+
+__device__ __forceinline__ void expm1d(const float (&a)[2], float dT, float (&r)[2]) {
+  const float m0 = dT * a[0];
+  const float m1 = dT * a[1];
+  float rel;  // (e^m0 - 1) / m0
+  if (fabsf(m0) > 1e-6f) {
+    rel = expm1f(m0) / m0;
+  } else {
+    const float sq = m0 * m0;
+    rel = 1.0f + 0.5f * m0 + (1.0f / 6.0f) * sq + (1.0f / 24.0f) * sq * m0;
+  }
+  r[0] = expf(m0);
+  r[1] = m1 * rel;
+}
+
+__device__ __forceinline__ void expm2d(const float (&a)[6], float dT, float (&r)[6]) {
+  float m[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) m[k] = dT * a[k];
+  const float nrm = sqrtf(m[0] * m[0] + m[1] * m[1] + m[2] * m[2] + m[3] * m[3] +
+                          m[4] * m[4] + m[5] * m[5]);
+  const int ns = squarings(nrm);
+  float sc = 1.0f;
+  for (int i = 0; i < ns; ++i) sc *= 0.5f;
+#pragma unroll
+  for (int k = 0; k < 6; ++k) m[k] *= sc;
+  // Rows of M^2 (the third row of M is zero).
+  const float s00 = m[0] * m[0] + m[1] * m[3];
+  const float s01 = m[0] * m[1] + m[1] * m[4];
+  const float s02 = m[0] * m[2] + m[1] * m[5];
+  const float s10 = m[3] * m[0] + m[4] * m[3];
+  const float s11 = m[3] * m[1] + m[4] * m[4];
+  const float s12 = m[3] * m[2] + m[4] * m[5];
+  const float c12 = 1.0f / 12.0f;
+  // Numerator N = I + M/2 + M^2/12, denominator D = I - M/2 + M^2/12.
+  const float n00 = 1.0f + 0.5f * m[0] + c12 * s00, d00 = 1.0f - 0.5f * m[0] + c12 * s00;
+  const float n01 = 0.5f * m[1] + c12 * s01, d01 = -0.5f * m[1] + c12 * s01;
+  const float n02 = 0.5f * m[2] + c12 * s02, d02 = -0.5f * m[2] + c12 * s02;
+  const float n10 = 0.5f * m[3] + c12 * s10, d10 = -0.5f * m[3] + c12 * s10;
+  const float n11 = 1.0f + 0.5f * m[4] + c12 * s11, d11 = 1.0f - 0.5f * m[4] + c12 * s11;
+  const float n12 = 0.5f * m[5] + c12 * s12, d12 = -0.5f * m[5] + c12 * s12;
+  // D^-1 = [Di, -Di d_t; 0 1] with Di the inverse of D's 2x2 linear block.
+  const float idet = 1.0f / (d00 * d11 - d01 * d10);
+  const float i00 = d11 * idet, i01 = -d01 * idet;
+  const float i10 = -d10 * idet, i11 = d00 * idet;
+  const float i02 = -(i00 * d02 + i01 * d12);
+  const float i12 = -(i10 * d02 + i11 * d12);
+  float r00 = i00 * n00 + i01 * n10, r01 = i00 * n01 + i01 * n11;
+  float r02 = i00 * n02 + i01 * n12 + i02;
+  float r10 = i10 * n00 + i11 * n10, r11 = i10 * n01 + i11 * n11;
+  float r12 = i10 * n02 + i11 * n12 + i12;
+  for (int i = 0; i < ns; ++i) {
+    const float t00 = r00 * r00 + r01 * r10, t01 = r00 * r01 + r01 * r11;
+    const float t02 = r00 * r02 + r01 * r12 + r02;
+    const float t10 = r10 * r00 + r11 * r10, t11 = r10 * r01 + r11 * r11;
+    const float t12 = r10 * r02 + r11 * r12 + r12;
+    r00 = t00; r01 = t01; r02 = t02; r10 = t10; r11 = t11; r12 = t12;
+  }
+  r[0] = r00; r[1] = r01; r[2] = r02; r[3] = r10; r[4] = r11; r[5] = r12;
+}
+
+__device__ __forceinline__ void expm3d(const float (&a)[12], float dT, float (&r)[12]) {
+  // L = linear 3x3 block, u = translation column, both scaled by dT.
+  float L[3][3], u[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) L[i][j] = dT * a[i * 4 + j];
+    u[i] = dT * a[i * 4 + 3];
+  }
+  const float nrm = sqrtf(L[0][0] * L[0][0] + L[0][1] * L[0][1] + L[0][2] * L[0][2] + u[0] * u[0] +
+                          L[1][0] * L[1][0] + L[1][1] * L[1][1] + L[1][2] * L[1][2] + u[1] * u[1] +
+                          L[2][0] * L[2][0] + L[2][1] * L[2][1] + L[2][2] * L[2][2] + u[2] * u[2]);
+  const int ns = squarings(nrm);
+  float sc = 1.0f;
+  for (int i = 0; i < ns; ++i) sc *= 0.5f;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) L[i][j] *= sc;
+    u[i] *= sc;
+  }
+  float S[3][3], su[3];  // M^2: linear block L*L and translation L*u
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) S[i][j] = L[i][0] * L[0][j] + L[i][1] * L[1][j] + L[i][2] * L[2][j];
+    su[i] = L[i][0] * u[0] + L[i][1] * u[1] + L[i][2] * u[2];
+  }
+  const float c12 = 1.0f / 12.0f;
+  float N[3][3], D[3][3], nu[3], du[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const float id = (i == j) ? 1.0f : 0.0f;
+      N[i][j] = (i == j) ? id + 0.5f * L[i][j] + c12 * S[i][j] : 0.5f * L[i][j] + c12 * S[i][j];
+      D[i][j] = (i == j) ? id - 0.5f * L[i][j] + c12 * S[i][j] : -0.5f * L[i][j] + c12 * S[i][j];
+    }
+    nu[i] = 0.5f * u[i] + c12 * su[i];
+    du[i] = -0.5f * u[i] + c12 * su[i];
+  }
+  // Inverse of D's linear block by cofactors.
+  const float det = D[0][0] * (D[1][1] * D[2][2] - D[1][2] * D[2][1]) -
+                    D[0][1] * (D[1][0] * D[2][2] - D[1][2] * D[2][0]) +
+                    D[0][2] * (D[1][0] * D[2][1] - D[1][1] * D[2][0]);
+  const float id = 1.0f / det;
+  float I[3][3];
+  I[0][0] = (D[1][1] * D[2][2] - D[1][2] * D[2][1]) * id;
+  I[0][1] = (D[0][2] * D[2][1] - D[0][1] * D[2][2]) * id;
+  I[0][2] = (D[0][1] * D[1][2] - D[0][2] * D[1][1]) * id;
+  I[1][0] = (D[1][2] * D[2][0] - D[1][0] * D[2][2]) * id;
+  I[1][1] = (D[0][0] * D[2][2] - D[0][2] * D[2][0]) * id;
+  I[1][2] = (D[0][2] * D[1][0] - D[0][0] * D[1][2]) * id;
+  I[2][0] = (D[1][0] * D[2][1] - D[1][1] * D[2][0]) * id;
+  I[2][1] = (D[0][1] * D[2][0] - D[0][0] * D[2][1]) * id;
+  I[2][2] = (D[0][0] * D[1][1] - D[0][1] * D[1][0]) * id;
+  float it[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) it[i] = -(I[i][0] * du[0] + I[i][1] * du[1] + I[i][2] * du[2]);
+  float R[3][3], ru[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) R[i][j] = I[i][0] * N[0][j] + I[i][1] * N[1][j] + I[i][2] * N[2][j];
+    ru[i] = I[i][0] * nu[0] + I[i][1] * nu[1] + I[i][2] * nu[2] + it[i];
+  }
+  for (int s = 0; s < ns; ++s) {
+    float Q[3][3], qu[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) Q[i][j] = R[i][0] * R[0][j] + R[i][1] * R[1][j] + R[i][2] * R[2][j];
+      qu[i] = R[i][0] * ru[0] + R[i][1] * ru[1] + R[i][2] * ru[2] + ru[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) R[i][j] = Q[i][j];
+      ru[i] = qu[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) r[i * 4 + j] = R[i][j];
+    r[i * 4 + 3] = ru[i];
+  }
+}
+
+template <int ND>
+__device__ __forceinline__ void expm_cell(const float (&a)[Dim<ND>::kPpc], float dT,
+                                          float (&r)[Dim<ND>::kPpc]) {
+  if constexpr (ND == 1) expm1d(a, dT, r);
+  else if constexpr (ND == 2) expm2d(a, dT, r);
+  else expm3d(a, dT, r);
+}
+
+template <int ND>
+__global__ void k_expm(const float *__restrict__ As, int64_t n, float dT, float *__restrict__ trels) {
+  constexpr int P = Dim<ND>::kPpc;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float a[P], r[P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) a[k] = __ldg(As + i * P + k);
+  expm_cell<ND>(a, dT, r);
+#pragma unroll
+  for (int k = 0; k < P; ++k) trels[i * P + k] = r[k];
+}
+
+// One thread per (transformation, cell): the cell's kPpc rows of B dotted with
+// theta, then (optionally) the cell's matrix exponential.
+template <int ND>
+__global__ void k_build_A(int64_t nC, int64_t d, int n_theta, const int32_t *__restrict__ rowptr,
+                          const int32_t *__restrict__ colidx, const float *__restrict__ vals,
+                          const float *__restrict__ theta, float dT, float *__restrict__ As,
+                          float *__restrict__ trels) {
+  constexpr int P = Dim<ND>::kPpc;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= nC * n_theta) return;
+  const int64_t t = i / nC;
+  const int64_t c = i - t * nC;
+  const float *th = theta + t * d;
+  float a[P];
+#pragma unroll
+  for (int r = 0; r < P; ++r) {
+    const int64_t row = c * P + r;
+    const int k0 = __ldg(rowptr + row), k1 = __ldg(rowptr + row + 1);
+    float s = 0.0f;
+    for (int k = k0; k < k1; ++k) s = fmaf(__ldg(vals + k), __ldg(th + __ldg(colidx + k)), s);
+    a[r] = s;
+  }
+#pragma unroll
+  for (int r = 0; r < P; ++r) As[i * P + r] = a[r];
+  if (trels != nullptr) {
+    float e[P];
+    expm_cell<ND>(a, dT, e);
+#pragma unroll
+    for (int r = 0; r < P; ++r) trels[i * P + r] = e[r];
+  }
+}
+
+// dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].
+__global__ void k_project(int64_t d, int64_t D, int n_theta, const int32_t *__restrict__ rowptr,
+                          const int32_t *__restrict__ colidx, const float *__restrict__ vals,
+                          const float *__restrict__ moments, float *__restrict__ dtheta) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= d * n_theta) return;
+  const int64_t j = i / n_theta;
+  const int64_t t = i - j * n_theta;
+  const float *m = moments + t * D;
+  const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
+  float s = 0.0f;
+  for (int k = k0; k < k1; ++k) s = fmaf(__ldg(vals + k), __ldg(m + __ldg(colidx + k)), s);
+  dtheta[t * d + j] = s;
+}
+
+constexpr int kThreads = 256;
+
+inline unsigned blocks_for(int64_t n) { return (unsigned)((n + kThreads - 1) / kThreads); }
+
+}  // namespace
+
+cudaError_t launch_expm(int ndim, const float *As, int64_t n, float dT, float *trels,
+                        cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  switch (ndim) {
+    case 1: k_expm<1><<<blocks_for(n), kThreads, 0, s>>>(As, n, dT, trels); break;
+    case 2: k_expm<2><<<blocks_for(n), kThreads, 0, s>>>(As, n, dT, trels); break;
+    default: k_expm<3><<<blocks_for(n), kThreads, 0, s>>>(As, n, dT, trels); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_t *rowptr,
+                           const int32_t *colidx, const float *vals, const float *theta,
+                           float dT, float *As, float *trels, cudaStream_t s) {
+  const int64_t n = nC * n_theta;
+  if (n == 0) return cudaSuccess;
+  switch (ndim) {
+    case 1:
+      k_build_A<1><<<blocks_for(n), kThreads, 0, s>>>(nC, d, n_theta, rowptr, colidx, vals, theta,
+                                                      dT, As, trels);
+      break;
+    case 2:
+      k_build_A<2><<<blocks_for(n), kThreads, 0, s>>>(nC, d, n_theta, rowptr, colidx, vals, theta,
+                                                      dT, As, trels);
+      break;
+    default:
+      k_build_A<3><<<blocks_for(n), kThreads, 0, s>>>(nC, d, n_theta, rowptr, colidx, vals, theta,
+                                                      dT, As, trels);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_project(int64_t d, int64_t D, int n_theta, const int32_t *rowptr,
+                           const int32_t *colidx, const float *vals, const float *moments,
+                           float *dtheta, cudaStream_t s) {
+  const int64_t n = d * n_theta;
+  if (n == 0) return cudaSuccess;
+  k_project<<<blocks_for(n), kThreads, 0, s>>>(d, D, n_theta, rowptr, colidx, vals, moments,
+                                               dtheta);
+  return cudaGetLastError();
+}
+
+}  // namespace cpab

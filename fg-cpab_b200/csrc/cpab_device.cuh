@@ -1,0 +1,349 @@
+// Device building blocks shared by the CPA kernels: tessellation cell lookup,
+// per-cell affine steps, cell-table staging and moment flushes.
+//
+// The cell rules and the step arithmetic are the reference's numerical
+// definitions (cpab/core/cpab_ops_{1,2,3}d.cu) restated with the same
+// floating-point operation sequence, so that trajectories and cell indices
+// agree bit for bit.  Only the way they are evaluated differs: floor() is done
+// with one round-down add on the FMA pipe instead of F2I/I2F conversions, and
+// cell tables are read from shared memory when they fit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cpab {
+
+// Steps between adjoint checkpoints; each segment is replayed into registers.
+constexpr int kSegSteps = 8;
+// Largest nstepsolver (reference: CPAB_MAX_STEPS = 100 in cpab_ops_2d.cuh:8).
+constexpr int kMaxSteps = 256;
+constexpr int kMaxSegs = kMaxSteps / kSegSteps;
+
+// Clamp bound of the 1D/2D lookups: 1 - 1e-7 rounded to float (= 1 - 2^-23).
+// cpab/core/cpab_ops_2d.cu:127-129, cpab/core/cpab_ops_1d.cu:92-93.
+constexpr float kOneMinusEps = 1.0f - 1e-7f;
+
+template <int ND> struct Dim {
+  static constexpr int kPpc = ND * (ND + 1);               // params per cell
+  static constexpr int kStride = ND == 1 ? 2 : (ND == 2 ? 8 : 12);  // smem floats per cell
+};
+
+// Tessellation geometry passed by value to kernels.
+struct Tess {
+  int nx, ny, nz;
+  float fx, fy, fz;    // (float)n*
+  float hx, hy, hz;    // 0.5f / (float)n*   (3D corner rule)
+};
+
+// floor(v) for 0 <= v < 2^22, as float and int, without conversion units:
+// v + 2^23 rounded toward -inf is 2^23 + floor(v) exactly.
+__device__ __forceinline__ float floor_nonneg(float v, int &i) {
+  const float r = __fadd_rd(v, 8388608.0f);
+  i = __float_as_int(r) - 0x4B000000;
+  return r - 8388608.0f;
+}
+
+// ---------------------------------------------------------------------------
+// Cell lookup.  Return the cell (interval / triangle / tetrahedron) index.
+// ---------------------------------------------------------------------------
+
+// 1D: interval index; cpab/core/cpab_ops_1d.cu:52-59.
+__device__ __forceinline__ int cell_of(const Tess &t, float x) {
+  const float xc = fminf(fmaxf(x, 0.0f), kOneMinusEps);
+  int i;
+  floor_nonneg(xc * t.fx, i);
+  return min(i, t.nx - 1);
+}
+
+// 2D: four triangles per square numbered bottom(0) right(1) top(2) left(3);
+// outside the unit square the triangle facing the nearest boundary part is
+// used.  cpab/core/cpab_ops_2d.cu:71-128 (the reference's `a*b - c`
+// comparisons are contracted to fma by nvcc; they are written as fmaf here).
+__device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
+  const float xc = fminf(fmaxf(px, 0.0f), kOneMinusEps);
+  const float yc = fminf(fmaxf(py, 0.0f), kOneMinusEps);
+  int ix, iy;
+  // xc * n < n for every n < 2^24 because xc <= 1 - 2^-23: no upper clamp.
+  const float fx0 = floor_nonneg(xc * t.fx, ix);
+  const float fy0 = floor_nonneg(yc * t.fy, iy);
+  const int base = (ix + iy * t.nx) << 2;
+  if (px <= 0.0f) {
+    if (py <= 0.0f && py * t.fy < px * t.fx) return base;
+    if (py >= 1.0f && fmaf(py, t.fy, -t.fy) > -px * t.fx) return base + 2;
+    return base + 3;
+  }
+  if (px >= 1.0f) {
+    if (py <= 0.0f && -py * t.fy > fmaf(px, t.fx, -t.fx)) return base;
+    if (py >= 1.0f && fmaf(py, t.fy, -t.fy) > fmaf(px, t.fx, -t.fx)) return base + 2;
+    return base + 1;
+  }
+  if (py <= 0.0f) return base;
+  if (py >= 1.0f) return base + 2;
+  const float lx = fmaf(xc, t.fx, -fx0);
+  const float ly = fmaf(yc, t.fy, -fy0);
+  const int upper_left = lx < ly;           // above the main diagonal
+  const int upper_right = (1.0f - lx) < ly;  // above the anti-diagonal
+  return base + ((upper_left * 3) ^ upper_right);
+}
+
+// 3D: five tetrahedra per cube (central one = 0), cube parity flips the
+// split; beyond a corner the coordinate with the smallest overshoot is moved
+// half a cell inside.  cpab/core/cpab_ops_3d.cu:67-131.
+__device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
+  const float ox = (fabsf(px - 0.5f) - 0.5f) * t.fx;
+  const float oy = (fabsf(py - 0.5f) - 0.5f) * t.fy;
+  const float oz = (fabsf(pz - 0.5f) - 0.5f) * t.fz;
+  if (ox > 0.0f && oy > 0.0f && oz > 0.0f) {
+    if (ox <= oy && ox <= oz) {
+      px = (px < 0.5f) ? t.hx : 1.0f - t.hx;
+    } else if (oy <= oz) {
+      py = (py < 0.5f) ? t.hy : 1.0f - t.hy;
+    } else {
+      pz = (pz < 0.5f) ? t.hz : 1.0f - t.hz;
+    }
+  }
+  const float sx = fminf(fmaxf(px, 0.0f), 1.0f) * t.fx;
+  const float sy = fminf(fmaxf(py, 0.0f), 1.0f) * t.fy;
+  const float sz = fminf(fmaxf(pz, 0.0f), 1.0f) * t.fz;
+  int i, j, k;
+  float fi = floor_nonneg(sx, i);
+  float fj = floor_nonneg(sy, j);
+  float fk = floor_nonneg(sz, k);
+  // A coordinate exactly on the upper face belongs to the last cube.
+  i = min(i, t.nx - 1); fi = fminf(fi, t.fx - 1.0f);
+  j = min(j, t.ny - 1); fj = fminf(fj, t.fy - 1.0f);
+  k = min(k, t.nz - 1); fk = fminf(fk, t.fz - 1.0f);
+  float x = sx - fi;
+  float y = sy - fj;
+  const float z = sz - fk;
+  int c = 5 * (i + t.nx * (j + t.ny * k));
+  if ((i ^ j ^ k) & 1) {  // odd cubes: rotate the local frame by 90 degrees
+    const float x0 = x;
+    x = y;
+    y = 1.0f - x0;
+  }
+  if (-x - y + z >= 0.0f) return c + 1;
+  if (x + y + z - 2.0f >= 0.0f) return c + 2;
+  if (-x + y - z >= 0.0f) return c + 3;
+  if (x - y - z >= 0.0f) return c + 4;
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// Cell tables.  A table holds kPpc floats per cell; in shared memory each
+// cell is padded to Dim<ND>::kStride floats so it loads with 128-bit LDS.
+// ---------------------------------------------------------------------------
+
+template <int ND, bool SMEM>
+__device__ __forceinline__ void load_cell(const float *__restrict__ tab, int c,
+                                          float (&m)[Dim<ND>::kPpc]) {
+  if constexpr (ND == 1) {
+    const float2 v = SMEM ? reinterpret_cast<const float2 *>(tab)[c]
+                          : __ldg(reinterpret_cast<const float2 *>(tab) + c);
+    m[0] = v.x; m[1] = v.y;
+  } else if constexpr (ND == 2) {
+    if constexpr (SMEM) {
+      const float4 *p = reinterpret_cast<const float4 *>(tab) + 2 * c;
+      const float4 u = p[0];
+      const float2 w = *reinterpret_cast<const float2 *>(p + 1);
+      m[0] = u.x; m[1] = u.y; m[2] = u.z; m[3] = u.w; m[4] = w.x; m[5] = w.y;
+    } else {
+      const float2 *p = reinterpret_cast<const float2 *>(tab) + 3 * c;
+      const float2 u = __ldg(p), v = __ldg(p + 1), w = __ldg(p + 2);
+      m[0] = u.x; m[1] = u.y; m[2] = v.x; m[3] = v.y; m[4] = w.x; m[5] = w.y;
+    }
+  } else {
+    const float4 *p = reinterpret_cast<const float4 *>(tab) + 3 * c;
+    const float4 u = SMEM ? p[0] : __ldg(p);
+    const float4 v = SMEM ? p[1] : __ldg(p + 1);
+    const float4 w = SMEM ? p[2] : __ldg(p + 2);
+    m[0] = u.x; m[1] = u.y; m[2] = u.z; m[3] = u.w;
+    m[4] = v.x; m[5] = v.y; m[6] = v.z; m[7] = v.w;
+    m[8] = w.x; m[9] = w.y; m[10] = w.z; m[11] = w.w;
+  }
+}
+
+// Copy nC cells of kPpc floats from global memory into a padded smem table.
+template <int ND>
+__device__ __forceinline__ void stage_table(float *__restrict__ s, const float *__restrict__ g,
+                                            int nC) {
+  constexpr int P = Dim<ND>::kPpc, S = Dim<ND>::kStride;
+  const int n = nC * P;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int c = i / P;
+    s[c * S + (i - c * P)] = __ldg(g + i);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Affine algebra on [ND] points with a row-major ND x (ND+1) matrix m.
+// v = m [p; 1] evaluated as the reference does: nested fmaf from the last
+// column inwards.
+// ---------------------------------------------------------------------------
+
+template <int ND>
+__device__ __forceinline__ void affine(const float (&m)[Dim<ND>::kPpc], const float (&p)[ND],
+                                       float (&v)[ND]) {
+#pragma unroll
+  for (int r = 0; r < ND; ++r) {
+    const float *row = m + r * (ND + 1);
+    float acc = row[ND];
+#pragma unroll
+    for (int k = ND - 1; k >= 0; --k) acc = __fmaf_rn(row[k], p[k], acc);
+    v[r] = acc;
+  }
+}
+
+template <int ND>
+__device__ __forceinline__ int lookup(const Tess &t, const float (&p)[ND]) {
+  if constexpr (ND == 1) return cell_of(t, p[0]);
+  else if constexpr (ND == 2) return cell_of(t, p[0], p[1]);
+  else return cell_of(t, p[0], p[1], p[2]);
+}
+
+// One midpoint (RK2) step inside cell matrix m:
+// p <- p + h v(p + h/2 v(p)).  cpab/core/cpab_ops_2d.cu:317-340.
+template <int ND>
+__device__ __forceinline__ void midpoint_step(const float (&m)[Dim<ND>::kPpc], float (&p)[ND],
+                                              float h, float h_half) {
+  float v[ND], q[ND], w[ND];
+  affine<ND>(m, p, v);
+#pragma unroll
+  for (int k = 0; k < ND; ++k) q[k] = __fmaf_rn(h_half, v[k], p[k]);
+  affine<ND>(m, q, w);
+#pragma unroll
+  for (int k = 0; k < ND; ++k) p[k] = __fmaf_rn(h, w[k], p[k]);
+}
+
+// Replay step of the adjoint: midpoint step in the start cell; when adaptive
+// and the step leaves the cell, a Heun step averaging the start and end cell
+// velocities replaces it.  Returns the start cell.
+// cpab/core/cpab_ops_2d.cu:342-380, cpab/core/cpab_ops_3d.cu:284-329.
+template <int ND, bool ADAPT, bool SMEM>
+__device__ __forceinline__ int replay_step(const Tess &t, const float *__restrict__ atab,
+                                           float (&p)[ND], float h, float h_half) {
+  const int c = lookup<ND>(t, p);
+  float m[Dim<ND>::kPpc];
+  load_cell<ND, SMEM>(atab, c, m);
+  if constexpr (!ADAPT) {
+    midpoint_step<ND>(m, p, h, h_half);
+  } else {
+    float q[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) q[k] = p[k];
+    midpoint_step<ND>(m, q, h, h_half);
+    const int ce = lookup<ND>(t, q);
+    if (ce == c) {
+#pragma unroll
+      for (int k = 0; k < ND; ++k) p[k] = q[k];
+    } else {
+      float v0[ND], v1[ND], me[Dim<ND>::kPpc];
+      affine<ND>(m, p, v0);
+      load_cell<ND, SMEM>(atab, ce, me);
+      affine<ND>(me, q, v1);
+#pragma unroll
+      for (int k = 0; k < ND; ++k) p[k] = __fmaf_rn(h_half, v0[k] + v1[k], p[k]);
+    }
+  }
+  return c;
+}
+
+// One reverse step of the adjoint of the midpoint rule in cell matrix m at
+// step start p: adds the step's contribution to the cell moments mo and moves
+// lam from t_{n+1} to t_n.  cpab/core/cpab_ops_2d.cu:382-430 (2D),
+// cpab/core/cpab_ops_3d.cu:331-403 (3D), cpab/core/cpab_ops_1d.cu:301-329 (1D).
+template <int ND>
+__device__ __forceinline__ void adjoint_step(const float (&m)[Dim<ND>::kPpc], const float (&p)[ND],
+                                             float (&lam)[ND], float (&mo)[Dim<ND>::kPpc],
+                                             float h, float h_half, float hh) {
+  constexpr int C = ND + 1;
+  float v[ND], q[ND], at[ND];
+  affine<ND>(m, p, v);
+#pragma unroll
+  for (int k = 0; k < ND; ++k) q[k] = __fmaf_rn(h_half, v[k], p[k]);
+  // at = A^T lam (linear part only)
+#pragma unroll
+  for (int k = 0; k < ND; ++k) {
+    float s = m[k] * lam[0];
+#pragma unroll
+    for (int r = 1; r < ND; ++r) s = s + m[r * C + k] * lam[r];
+    at[k] = s;
+  }
+  float wq[ND], wp[ND];
+#pragma unroll
+  for (int r = 0; r < ND; ++r) { wq[r] = h * lam[r]; wp[r] = hh * at[r]; }
+#pragma unroll
+  for (int r = 0; r < ND; ++r) {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) mo[r * C + k] += wq[r] * q[k];
+    mo[r * C + ND] += wq[r];
+  }
+#pragma unroll
+  for (int r = 0; r < ND; ++r) {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) mo[r * C + k] += wp[r] * p[k];
+    mo[r * C + ND] += wp[r];
+  }
+  float lm[ND];
+#pragma unroll
+  for (int k = 0; k < ND; ++k) lm[k] = lam[k] + h_half * at[k];
+#pragma unroll
+  for (int k = 0; k < ND; ++k) {
+    float s = m[k] * lm[0];
+#pragma unroll
+    for (int r = 1; r < ND; ++r) s = s + m[r * C + k] * lm[r];
+    lam[k] += h * s;
+  }
+}
+
+// Flush one cell's partial moments into a shared-memory table.
+template <int P>
+__device__ __forceinline__ void flush_smem(float *__restrict__ s_mom, int c, float (&mo)[P]) {
+  float *dst = s_mom + c * P;
+#pragma unroll
+  for (int k = 0; k < P; ++k) {
+    atomicAdd(dst + k, mo[k]);
+    mo[k] = 0.0f;
+  }
+}
+
+// Flush one cell's partial moments straight to global memory.  Lanes of the
+// warp that flush the same cell are summed first, so each cell costs one
+// atomic per moment per warp.
+template <int P>
+__device__ __forceinline__ void flush_global(float *__restrict__ g_mom, int c, float (&mo)[P]) {
+  const unsigned active = __activemask();
+  const unsigned same = __match_any_sync(active, c);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(same) - 1;
+  if (same != (1u << lane)) {
+    // Sum the group's values into the leader, one peer at a time.
+    unsigned rest = same & ~(1u << leader);
+    float acc[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) acc[k] = mo[k];
+    while (rest) {
+      const int src = __ffs(rest) - 1;
+      rest &= rest - 1;
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const float v = __shfl_sync(same, mo[k], src);
+        acc[k] += v;
+      }
+    }
+    if (lane == leader) {
+      float *dst = g_mom + (int64_t)c * P;
+#pragma unroll
+      for (int k = 0; k < P; ++k) atomicAdd(dst + k, acc[k]);
+    }
+  } else {
+    float *dst = g_mom + (int64_t)c * P;
+#pragma unroll
+    for (int k = 0; k < P; ++k) atomicAdd(dst + k, mo[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < P; ++k) mo[k] = 0.0f;
+}
+
+}  // namespace cpab

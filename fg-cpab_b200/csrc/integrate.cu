@@ -1,0 +1,431 @@
+// CPA trajectory integration on sm_100a: forward (1D closed form, 2D/3D
+// exact per-cell steps) and the fused factorized-adjoint backward.
+//
+// Design (one CUDA thread per (point, transformation) pair, as in the
+// reference, but):
+//   * grids are sized to one resident wave (occupancy x SM count); blocks
+//     stride over the points of one transformation, so the per-transformation
+//     cell tables are staged into shared memory once per block, not per 256
+//     points;
+//   * cell tables live in shared memory when they fit (padded to 128-bit
+//     rows), else they are read through the read-only cache with vector loads;
+//   * the adjoint keeps each replayed 8-step segment in registers (fully
+//     unrolled), checkpoints every 8 steps, and flushes per-cell moments into
+//     a block-wide shared-memory moment table that is written to global memory
+//     once per block -- instead of per-crossing global atomics.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "launch.h"
+
+namespace cpab {
+
+namespace {
+
+constexpr int kFwdThreads = 256;
+constexpr int kBwdThreads = 256;
+// Shared-memory budget per block; two blocks per SM keep 16+ warps resident.
+constexpr size_t kFwdSmemBudget = 100 * 1024;
+constexpr size_t kBwdSmemBudget = 110 * 1024;
+
+// ---------------------------------------------------------------------------
+// 1D closed form.  cpab/core/cpab_ops_1d.cu:103-205.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int sgn(float x) { return (x > 0.0f) - (x < 0.0f); }
+__device__ __forceinline__ bool near0(float x) { return fabsf(x) < 1e-7f; }
+
+// Time for the flow x' = a x + b started at x in cell c to reach the facet it
+// moves towards (shifted 1e-7 past it); +-inf when it never does.  Writes the
+// hit position and the next cell.
+__device__ __forceinline__ float hit_time_1d(float x, float t, int c, float a, float b, int nx,
+                                             float fnx, float &xc, int &cc) {
+  const int s = sgn(t);
+  const float never = INFINITY * (float)s;
+  const float v = __fmaf_rn(a, x, b);
+  if (near0(v)) return never;
+  cc = c + sgn(v) * s;
+  if (cc < 0 || cc >= nx) return never;
+  // Moving right in time-forward direction exits through the right facet.
+  if ((v > 0.0f) == (t > 0.0f)) xc = ((float)(c + 1) / fnx) + 1e-7f;
+  else xc = ((float)c / fnx) - 1e-7f;
+  const float vc = __fmaf_rn(a, xc, b);
+  if (near0(vc)) return never;
+  if (sgn(v) != sgn(vc)) return never;
+  if (xc <= 0.0f || xc >= 1.0f) return never;
+  if (near0(a)) return (xc - x) / b;
+  return logf(vc / v) / a;
+}
+
+// psi(x, t) = e^{ta} (x + b/a) - b/a  (x + t b when a ~ 0).
+__device__ __forceinline__ float flow_1d(float x, float t, float a, float b) {
+  if (near0(a)) return __fmaf_rn(t, b, x);
+  const float ba = b / a;
+  return __fmaf_rn(expf(t * a), x + ba, -ba);
+}
+
+template <bool SMEM>
+__global__ void __launch_bounds__(kFwdThreads) k_forward_1d(IntegrateArgs a) {
+  extern __shared__ float4 smem4[];
+  float *s_tab = reinterpret_cast<float *>(smem4);
+  const int b = blockIdx.y;
+  const float *ag = a.As + (int64_t)b * a.nC * 2;
+  if constexpr (SMEM) {
+    for (int i = threadIdx.x; i < a.nC * 2; i += blockDim.x) s_tab[i] = __ldg(ag + i);
+    __syncthreads();
+  }
+  const float2 *tab = reinterpret_cast<const float2 *>(SMEM ? s_tab : ag);
+  const float *pin = a.points + (a.batched ? (int64_t)b * a.nP : 0);
+  float *pout = a.out + (int64_t)b * a.nP;
+  const Tess t = a.tess;
+  const int nx = t.nx;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < a.nP;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float x = __ldg(pin + i);
+    float tr = 1.0f;
+    int c = cell_of(t, x);
+    const int max_hops = max(c, nx - 1 - c) + 1;
+    int hops = 0;
+    float res;
+    while (true) {
+      const float2 ab = SMEM ? tab[c] : __ldg(tab + c);
+      float xc = x;
+      int cc = c;
+      const float th = hit_time_1d(x, tr, c, ab.x, ab.y, nx, t.fx, xc, cc);
+      const float sf = (float)sgn(tr);
+      if (sf * th > sf * tr) {
+        res = flow_1d(x, tr, ab.x, ab.y);
+        break;
+      }
+      x = xc;
+      c = cc;
+      tr -= th;
+      if (++hops > max_hops) {
+        res = x;
+        break;
+      }
+    }
+    pout[i] = res;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2D/3D forward: T exact steps p <- Trels[cell(p)] [p;1].
+// cpab/core/cpab_ops_2d.cu:212-278, cpab/core/cpab_ops_3d.cu:169-241.
+// ---------------------------------------------------------------------------
+
+template <int ND, bool ADAPT, bool SMEM>
+__global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
+  constexpr int P = Dim<ND>::kPpc;
+  extern __shared__ float4 smem4[];
+  float *s_tab = reinterpret_cast<float *>(smem4);
+  const int b = blockIdx.y;
+  const float *tg = a.trels + (int64_t)b * a.nC * P;
+  const float *ag = a.As + (int64_t)b * a.nC * P;
+  if constexpr (SMEM) {
+    stage_table<ND>(s_tab, tg, a.nC);
+    __syncthreads();
+  }
+  const float *tab = SMEM ? s_tab : tg;
+  const Tess t = a.tess;
+  const int T = a.T;
+  const float h_half = 0.5f * (1.0f / (float)T);
+  const int64_t nP = a.nP;
+  const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
+  float *pout = a.out + (int64_t)b * ND * nP;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+#pragma unroll 2
+    for (int n = 0; n < T; ++n) {
+      const int c = lookup<ND>(t, p);
+      float m[P];
+      load_cell<ND, SMEM>(tab, c, m);
+      float q[ND];
+      affine<ND>(m, p, q);
+      if constexpr (ADAPT) {
+        const int ce = lookup<ND>(t, q);
+        if (ce != c) {  // Heun step across the facet
+          float m0[P], m1[P], v0[ND], v1[ND];
+          load_cell<ND, false>(ag, c, m0);
+          load_cell<ND, false>(ag, ce, m1);
+          affine<ND>(m0, p, v0);
+          affine<ND>(m1, q, v1);
+#pragma unroll
+          for (int k = 0; k < ND; ++k) p[k] = __fmaf_rn(h_half, v0[k] + v1[k], p[k]);
+          continue;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < ND; ++k) p[k] = q[k];
+    }
+#pragma unroll
+    for (int k = 0; k < ND; ++k) pout[k * nP + i] = p[k];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused adjoint backward.  cpab/core/cpab_ops_2d.cu:432-561 (2D),
+// cpab/core/cpab_ops_3d.cu:405-532 (3D), cpab/core/cpab_ops_1d.cu:331-422 (1D).
+// ---------------------------------------------------------------------------
+
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM>
+__global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
+  constexpr int P = Dim<ND>::kPpc;
+  constexpr int S = kSegSteps;
+  extern __shared__ float4 smem4[];
+  float *s_tab = reinterpret_cast<float *>(smem4);
+  float *s_mom = s_tab + (A_SMEM ? a.nC * Dim<ND>::kStride : 0);
+  const int b = blockIdx.y;
+  const int nC = a.nC;
+  const float *ag = a.As + (int64_t)b * nC * P;
+  float *gm = a.moments + (int64_t)b * nC * P;
+  if constexpr (A_SMEM) stage_table<ND>(s_tab, ag, nC);
+  if constexpr (M_SMEM) {
+    for (int i = threadIdx.x; i < nC * P; i += blockDim.x) s_mom[i] = 0.0f;
+  }
+  if constexpr (A_SMEM || M_SMEM) __syncthreads();
+  const float *tab = A_SMEM ? s_tab : ag;
+  float *mom = M_SMEM ? s_mom : gm;
+
+  const Tess t = a.tess;
+  const int T = a.T;
+  const float h = 1.0f / (float)T;
+  const float h_half = h * 0.5f;
+  const float hh = h_half * h;
+  const int nseg = (T + S - 1) / S;
+  const int64_t nP = a.nP;
+  const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
+  const float *gin = a.grad_out + (int64_t)b * ND * nP;
+  float *gp = a.grad_points ? a.grad_points + (int64_t)b * ND * nP : nullptr;
+
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+
+    // Phase 1: midpoint replay, keeping the start of every segment.
+    float ck[kMaxSegs][ND];
+    for (int seg = 0; seg < nseg; ++seg) {
+#pragma unroll
+      for (int k = 0; k < ND; ++k) ck[seg][k] = p[k];
+      const int len = min(S, T - seg * S);
+#pragma unroll
+      for (int s = 0; s < S; ++s)
+        if (s < len) replay_step<ND, ADAPT, A_SMEM>(t, tab, p, h, h_half);
+    }
+
+    // Phase 2: segments last to first; replay into registers, then walk back.
+    float lam[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) lam[k] = __ldg(gin + k * nP + i);
+    float mo[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) mo[k] = 0.0f;
+    int prev = -1;
+    for (int seg = nseg - 1; seg >= 0; --seg) {
+      const int len = min(S, T - seg * S);
+      float xs[S][ND];
+      int cs[S];
+#pragma unroll
+      for (int k = 0; k < ND; ++k) p[k] = ck[seg][k];
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        if (s < len) {
+#pragma unroll
+          for (int k = 0; k < ND; ++k) xs[s][k] = p[k];
+          cs[s] = replay_step<ND, ADAPT, A_SMEM>(t, tab, p, h, h_half);
+        }
+      }
+#pragma unroll
+      for (int s = S - 1; s >= 0; --s) {
+        if (s < len) {
+          const int c = cs[s];
+          if (c != prev) {
+            if (prev >= 0) {
+              if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
+              else flush_global<P>(mom, prev, mo);
+            }
+            prev = c;
+          }
+          float m[P];
+          load_cell<ND, A_SMEM>(tab, c, m);
+          adjoint_step<ND>(m, xs[s], lam, mo, h, h_half, hh);
+        }
+      }
+    }
+    if (prev >= 0) {
+      if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
+      else flush_global<P>(mom, prev, mo);
+    }
+    if (gp) {
+#pragma unroll
+      for (int k = 0; k < ND; ++k) gp[k * nP + i] = lam[k];
+    }
+  }
+
+  if constexpr (M_SMEM) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < nC * P; i += blockDim.x) {
+      const float v = s_mom[i];
+      if (v != 0.0f) atomicAdd(gm + i, v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Cell lookup of a point set (the lookup the integrators use, exposed).
+// ---------------------------------------------------------------------------
+
+template <int ND>
+__global__ void k_cell_index(Tess t, const float *__restrict__ pts, int64_t n,
+                             int32_t *__restrict__ cells) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(pts + k * n + i);
+    cells[i] = lookup<ND>(t, p);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launch helpers.
+// ---------------------------------------------------------------------------
+
+// Resident blocks per SM for (kernel, threads, smem), cached per device.  The
+// first query of a kernel on a device also raises its dynamic shared-memory
+// limit to the device maximum.
+int blocks_per_sm(const void *kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  static std::unordered_map<uint64_t, bool> raised;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t kkey = (reinterpret_cast<uint64_t>(kernel) << 6) ^ (uint64_t)dev;
+  const uint64_t key = kkey * 1000003ull ^ (smem << 10) ^ (uint64_t)threads;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!raised[kkey]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         device_info().max_smem_optin);
+    raised[kkey] = true;
+  }
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess ||
+      n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// One resident wave: blocks along x stride over the points of one
+// transformation (blockIdx.y).
+dim3 wave_grid(const void *kernel, int threads, size_t smem, int64_t nP, int n_theta) {
+  const int64_t cap = (int64_t)blocks_per_sm(kernel, threads, smem) * device_info().sm_count;
+  const int64_t need = (nP + threads - 1) / threads;
+  int64_t nbx = cap / n_theta;
+  if (nbx < 1) nbx = 1;
+  if (nbx > need) nbx = need;
+  return dim3((unsigned)nbx, (unsigned)n_theta);
+}
+
+template <typename K>
+cudaError_t launch_wave(K kernel, int threads, size_t smem, const IntegrateArgs &a,
+                        cudaStream_t s) {
+  const void *kp = reinterpret_cast<const void *>(kernel);
+  const dim3 grid = wave_grid(kp, threads, smem, a.nP, a.n_theta);
+  kernel<<<grid, threads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int ND>
+cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
+  const size_t tab = (size_t)a.nC * Dim<ND>::kStride * sizeof(float);
+  const bool smem = tab <= kFwdSmemBudget;
+  if (a.adaptive) {
+    return smem ? launch_wave(k_forward<ND, true, true>, kFwdThreads, tab, a, s)
+                : launch_wave(k_forward<ND, true, false>, kFwdThreads, 0, a, s);
+  }
+  return smem ? launch_wave(k_forward<ND, false, true>, kFwdThreads, tab, a, s)
+              : launch_wave(k_forward<ND, false, false>, kFwdThreads, 0, a, s);
+}
+
+template <int ND, bool ADAPT>
+cudaError_t backward_nd(const IntegrateArgs &a, cudaStream_t s) {
+  const size_t tab = (size_t)a.nC * Dim<ND>::kStride * sizeof(float);
+  const size_t mom = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  if (tab + mom <= kBwdSmemBudget)
+    return launch_wave(k_backward<ND, ADAPT, true, true>, kBwdThreads, tab + mom, a, s);
+  if (mom <= kBwdSmemBudget)
+    return launch_wave(k_backward<ND, ADAPT, false, true>, kBwdThreads, mom, a, s);
+  return launch_wave(k_backward<ND, ADAPT, false, false>, kBwdThreads, 0, a, s);
+}
+
+}  // namespace
+
+const DeviceInfo &device_info() {
+  static DeviceInfo info[64];
+  static bool init[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    info[dev].sm_count = v > 0 ? v : 1;
+    v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    info[dev].max_smem_optin = v > 0 ? v : 48 * 1024;
+    init[dev] = true;
+  }
+  return info[dev];
+}
+
+cudaError_t launch_cell_index(int ndim, Tess t, const float *points, int64_t n, int32_t *cells,
+                              cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  const int64_t cap = (int64_t)device_info().sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  switch (ndim) {
+    case 1: k_cell_index<1><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
+    case 2: k_cell_index<2><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
+    default: k_cell_index<3><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_forward_1d(const IntegrateArgs &a, cudaStream_t s) {
+  const size_t tab = (size_t)a.nC * 2 * sizeof(float);
+  if (tab <= kFwdSmemBudget) return launch_wave(k_forward_1d<true>, kFwdThreads, tab, a, s);
+  return launch_wave(k_forward_1d<false>, kFwdThreads, 0, a, s);
+}
+
+cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s) {
+  switch (a.ndim) {
+    case 1: return launch_forward_1d(a, s);
+    case 2: return forward_nd<2>(a, s);
+    default: return forward_nd<3>(a, s);
+  }
+}
+
+cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s) {
+  switch (a.ndim) {
+    case 1: return a.adaptive ? backward_nd<1, true>(a, s) : backward_nd<1, false>(a, s);
+    case 2: return a.adaptive ? backward_nd<2, true>(a, s) : backward_nd<2, false>(a, s);
+    default: return a.adaptive ? backward_nd<3, true>(a, s) : backward_nd<3, false>(a, s);
+  }
+}
+
+}  // namespace cpab

@@ -1,0 +1,69 @@
+// Internal launch interface between the C ABI layer (capi.cu) and the kernel
+// translation units.  Arguments here are already validated.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cpab_device.cuh"
+
+namespace cpab {
+
+struct IntegrateArgs {
+  int ndim;
+  Tess tess;
+  int nC;
+  const float *points;  // [ndim, nP] or [n_theta, ndim, nP]
+  int64_t nP;
+  int batched;
+  const float *trels;   // [n_theta, nC, ppc] (forward 2D/3D)
+  const float *As;      // [n_theta, nC, ppc]
+  int n_theta;
+  int T;                // nstepsolver
+  int adaptive;
+  const float *grad_out;  // backward: [n_theta, ndim, nP]
+  float *out;             // forward: [n_theta, ndim, nP]
+  float *moments;         // backward: [n_theta, nC, ppc]
+  float *grad_points;     // backward: [n_theta, ndim, nP] or nullptr
+};
+
+// Each returns cudaSuccess or the launch error.
+cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s);
+cudaError_t launch_forward_1d(const IntegrateArgs &a, cudaStream_t s);
+cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s);
+
+cudaError_t launch_cell_index(int ndim, Tess t, const float *points, int64_t n, int32_t *cells,
+                              cudaStream_t s);
+cudaError_t launch_expm(int ndim, const float *As, int64_t n, float dT, float *trels,
+                        cudaStream_t s);
+cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_t *rowptr,
+                           const int32_t *colidx, const float *vals, const float *theta,
+                           float dT, float *As, float *trels, cudaStream_t s);
+cudaError_t launch_project(int64_t d, int64_t D, int n_theta, const int32_t *rowptr,
+                           const int32_t *colidx, const float *vals, const float *moments,
+                           float *dtheta, cudaStream_t s);
+
+struct ResampleArgs {
+  int ndim;
+  const float *data;
+  int n_batch, n_channels;
+  int64_t in_size[3];
+  const float *grid;
+  int64_t out_size[3];
+  float *out;              // forward
+  const float *grad_out;   // backward
+  float *grad_grid;        // backward, may be null
+  float *grad_data;        // backward, may be null (zeroed by the caller)
+};
+
+cudaError_t launch_interpolate(const ResampleArgs &a, cudaStream_t s);
+cudaError_t launch_interpolate_backward(const ResampleArgs &a, cudaStream_t s);
+
+// Device properties cached per device (SM count, opt-in shared memory).
+struct DeviceInfo {
+  int sm_count;
+  int max_smem_optin;
+};
+const DeviceInfo &device_info();
+
+}  // namespace cpab

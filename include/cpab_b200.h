@@ -1,0 +1,175 @@
+/*
+ * cpab_b200.h -- C ABI of the sm_100a implementation of the FG-CPAB hot path.
+ *
+ * The library (libcpab_b200.so) integrates points through continuous
+ * piecewise-affine (CPA) velocity fields in 1D/2D/3D, runs the factorized
+ * adjoint sweep that produces per-cell moments, projects the moments onto the
+ * CPA basis (dtheta = B^T vec(M)) and resamples images/volumes on warped grids.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers to contiguous fp32 / int32 arrays; the
+ *     caller owns every buffer.  Nothing here allocates device memory.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and is asynchronous with respect to the host.
+ *   - The return value is CPAB_OK (0) or a negative cpab_status.  Argument
+ *     errors are detected on the host before anything is launched; the message
+ *     is available from cpab_b200_last_error() (per host thread).  No entry
+ *     point ever terminates the process.
+ *   - Layouts follow the reference extension: points are [ndim, nP] (shared by
+ *     all transformations) or [n_theta, ndim, nP]; affine cell matrices are
+ *     [n_theta, nC, ndim, ndim+1] row-major; moments are [n_theta, nC, ppc]
+ *     with ppc = ndim*(ndim+1).
+ *   - Cell-matrix tables (As, trels) must be 16-byte aligned (they are read
+ *     with vector loads); every other array only needs its natural alignment.
+ *   - Tessellation: nc[0..ndim-1] cells per axis (1 <= nc[k] <= 2^20) on
+ *     [0,1]^ndim; nC = nc[0]
+ *     (1D), 4*nc[0]*nc[1] (2D, four triangles per square), 5*nc[0]*nc[1]*nc[2]
+ *     (3D, five tetrahedra per cube).
+ *
+ * Reference interfaces replaced (paths inside the FG-CPAB project):
+ *   cpab/pytorch/transformer_cuda.cpp:32-61   forward               -> cpab_b200_forward
+ *   cpab/pytorch/transformer_cuda.cpp:66-85   forward_1d_closed_form -> cpab_b200_forward_1d_closed_form
+ *   cpab/pytorch/transformer_cuda.cpp:92-116  backward_moments      -> cpab_b200_backward (grad_points = NULL)
+ *   cpab/pytorch/transformer_cuda.cpp:122-153 backward_moments_and_points -> cpab_b200_backward
+ *   cpab/pytorch/transformer_cuda.cpp:159-170 expm                  -> cpab_b200_expm
+ *   cpab/pytorch/transformer.py:84-88         A = B theta^T (torch.sparse.mm) -> cpab_b200_build_A
+ *   cpab/pytorch/transformer.py:165-166       dtheta = B^T m (torch.sparse.mm) -> cpab_b200_project
+ *   cpab/pytorch/interpolation.py:8-160       interpolate{1,2,3}D (+autograd) -> cpab_b200_interpolate{,_backward}
+ */
+#ifndef CPAB_B200_H
+#define CPAB_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *cpab_stream_t; /* identical to cudaStream_t */
+
+typedef enum {
+  CPAB_OK = 0,
+  CPAB_ERR_ARG = -1,    /* invalid shape / pointer / flag                 */
+  CPAB_ERR_STEPS = -2,  /* nstepsolver outside [1, cpab_b200_max_steps()] */
+  CPAB_ERR_CUDA = -3,   /* a CUDA launch or runtime call failed           */
+  CPAB_ERR_SIZE = -4    /* a size exceeds a documented limit              */
+} cpab_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int cpab_b200_version(void);
+
+/* Largest nstepsolver accepted by forward/backward (the reference allows 100). */
+int cpab_b200_max_steps(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char *cpab_b200_last_error(void);
+
+/*
+ * Trels[i] = expm(dT * [A_i; 0 ... 0 1]) restricted to its top ndim rows, for
+ * n affine matrices A_i of shape [ndim, ndim+1].  Scaling-and-squaring with
+ * the (2,2) Pade approximant in 2D/3D; closed form [e^a, b*(e^a-1)/a] in 1D.
+ * Replaces cpab/pytorch/transformer_cuda.cpp:159-170 (cpab_expm).
+ */
+int cpab_b200_expm(int ndim, const float *As, int64_t n_matrices, float dT,
+                   float *trels, cpab_stream_t stream);
+
+/*
+ * A = reshape((B theta^T)^T): As[t, r] = sum_k B[r, k] * theta[t, k] for the
+ * D x d CSR basis B (D = nC*ppc rows).  When trels != NULL also writes
+ * trels = expm(dT * A) per cell (same rule as cpab_b200_expm), fused.
+ * Replaces cpab/pytorch/transformer.py:84-88 and :104-106.
+ */
+int cpab_b200_build_A(int ndim, int64_t nC, int64_t d, int n_theta,
+                      const int32_t *B_rowptr, const int32_t *B_colidx,
+                      const float *B_vals, const float *theta, float dT,
+                      float *As, float *trels, cpab_stream_t stream);
+
+/*
+ * Forward integration to t = 1 in 2D/3D: nstepsolver exact per-cell steps
+ * p <- trels[cell(p)] [p; 1]; with adaptive = 1 a step that changes cell is
+ * replaced by one Heun step on the velocity fields As.  `points_batched` = 1
+ * when points is [n_theta, ndim, nP], 0 when it is [ndim, nP].  out is
+ * [n_theta, ndim, nP].  nc has ndim entries.  For ndim == 1 this forwards to
+ * cpab_b200_forward_1d_closed_form (trels and nstepsolver are then unused),
+ * like the reference's dispatch.
+ * Replaces cpab/pytorch/transformer_cuda.cpp:32-61 (cpab_forward).
+ */
+int cpab_b200_forward(int ndim, const int32_t *nc, const float *points,
+                      int64_t nP, int points_batched, const float *trels,
+                      const float *As, int n_theta, int nstepsolver,
+                      int adaptive, float *out, cpab_stream_t stream);
+
+/*
+ * Exact 1D CPA integration to t = 1 (analytic cell walk, no time stepping).
+ * Replaces cpab/pytorch/transformer_cuda.cpp:66-85.
+ */
+int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP,
+                                     int points_batched, const float *As,
+                                     int n_theta, int ncx, float *out,
+                                     cpab_stream_t stream);
+
+/*
+ * Factorized adjoint sweep.  Replays every trajectory with the midpoint rule
+ * (nstepsolver steps, Heun on crossings when adaptive = 1), walks it backwards
+ * from lambda(1) = grad_out and accumulates the per-cell moments
+ *   M_c += h lam p_mid^T + (h^2/2) (A_c^T lam) p^T    (as [n_theta, nC, ppc]).
+ * moments is overwritten (zeroed here first).  When grad_points != NULL it
+ * receives lambda(0) as [n_theta, ndim, nP] (the reference's grad_points
+ * before its optional batch sum).
+ * Replaces cpab/pytorch/transformer_cuda.cpp:92-116 and :122-153.
+ */
+int cpab_b200_backward(int ndim, const int32_t *nc, const float *points,
+                       int64_t nP, int points_batched, const float *As,
+                       int n_theta, const float *grad_out, int nstepsolver,
+                       int adaptive, float *moments, float *grad_points,
+                       cpab_stream_t stream);
+
+/*
+ * cells[i] = index of the tessellation cell containing points[:, i]
+ * (points [ndim, n]); outside the domain, the cell the integrators use there.
+ * Replaces the device lookups cuda_findcellidx_{1D,2D,3D}_fast of
+ * cpab/core/cpab_ops_1d.cu:90-97, cpab/core/cpab_ops_2d.cu:119-176 and
+ * cpab/core/cpab_ops_3d.cu:67-131 (same rule, bit for bit).
+ */
+int cpab_b200_cell_index(int ndim, const int32_t *nc, const float *points,
+                         int64_t n, int32_t *cells, cpab_stream_t stream);
+
+/*
+ * dtheta[t, j] = sum_i Bt[j, i] * moments[t, i] for the d x D CSR matrix
+ * Bt = B^T.  dtheta is [n_theta, d] and is overwritten.
+ * Replaces cpab/pytorch/transformer.py:165-166.
+ */
+int cpab_b200_project(int64_t d, int64_t D, int n_theta,
+                      const int32_t *Bt_rowptr, const int32_t *Bt_colidx,
+                      const float *Bt_vals, const float *moments,
+                      float *dtheta, cpab_stream_t stream);
+
+/*
+ * Linear / bilinear / trilinear resampling of data [n_batch, C, *in_size] at
+ * grid [n_batch, ndim, P] (P = prod(out_size), coordinate 0 fastest; grid
+ * coordinate k indexes data axis 2+k after scaling by in_size[k]-1, border
+ * clamped).  out is [n_batch, C, *out_size].
+ * Replaces cpab/pytorch/interpolation.py:8-160 (forward).
+ */
+int cpab_b200_interpolate(int ndim, const float *data, int n_batch,
+                          int n_channels, const int64_t *in_size,
+                          const float *grid, const int64_t *out_size,
+                          float *out, cpab_stream_t stream);
+
+/*
+ * Backward of cpab_b200_interpolate.  grad_grid ([n_batch, ndim, P], may be
+ * NULL) is overwritten; grad_data ([n_batch, C, *in_size], may be NULL) is
+ * zeroed and then receives the scatter-add of the interpolation weights.
+ * Replaces the torch autograd graph of cpab/pytorch/interpolation.py:8-160.
+ */
+int cpab_b200_interpolate_backward(int ndim, const float *data, int n_batch,
+                                   int n_channels, const int64_t *in_size,
+                                   const float *grid, const int64_t *out_size,
+                                   const float *grad_out, float *grad_grid,
+                                   float *grad_data, cpab_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CPAB_B200_H */

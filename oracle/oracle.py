@@ -1,0 +1,266 @@
+"""CPU parity oracle for the FG-CPAB hot path.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline legs of bench.py, as the checker -- never by the product.
+
+  * integration / adjoint / expm / cell lookup: liboracle.so, the C
+    restatement in cpab_oracle.c (cpab/core/cpab_ops_{1,2,3}d.cu);
+  * A = B theta and dtheta = B^T m: scipy sparse products in float64, rounded
+    to float32 (cpab/pytorch/transformer.py:84-88, :165-166 use
+    torch.sparse.mm);
+  * resampling: numpy float32 restatement of cpab/pytorch/interpolation.py:8-160
+    (forward, op for op) and of the gradient its autograd graph produces.
+
+Pinned against the reference by the golden fixtures in tests/golden/ (basis
+and interpolation from the reference's Python run on CPU; kernel outputs from
+the reference's CUDA kernels built into oracle/_ref and run on a B200).
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+_c_int, _c_i64, _c_f, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            import importlib.util
+            spec = importlib.util.spec_from_file_location(
+                "build_oracle", os.path.join(HERE, "build_oracle.py"))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            mod.build_oracle()
+        L = ctypes.CDLL(LIB_PATH)
+        L.oracle_cells.argtypes = [_c_int, _p, _p, _c_i64, _p]
+        L.oracle_expm.argtypes = [_c_int, _p, _c_i64, _c_f, _p]
+        L.oracle_forward.argtypes = [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _c_int, _c_int, _p]
+        L.oracle_backward.argtypes = [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _p, _c_int, _c_int,
+                                      _p, _p]
+        L.oracle_midpoint_forward.argtypes = [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _c_int,
+                                              _c_int, _p]
+        L.oracle_midpoint_forward.restype = None
+        L.oracle_num_threads.restype = _c_int
+        L.oracle_set_num_threads.argtypes = [_c_int]
+        for fn in (L.oracle_cells, L.oracle_expm, L.oracle_forward, L.oracle_backward):
+            fn.restype = None
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else ctypes.c_void_p(0)
+
+
+def _nc(nc):
+    return np.ascontiguousarray(nc, dtype=np.int32)
+
+
+def num_threads():
+    return lib().oracle_num_threads()
+
+
+def set_num_threads(n):
+    lib().oracle_set_num_threads(int(n))
+
+
+def n_cells(nc):
+    k = int(np.prod(nc))
+    return {1: k, 2: 4 * k, 3: 5 * k}[len(nc)]
+
+
+def cells(nc, points):
+    """Cell index of every point, points [ndim, n] -> int32 [n]."""
+    pts = _f32(points)
+    nd, n = pts.shape
+    out = np.empty(n, dtype=np.int32)
+    nca = _nc(nc)
+    lib().oracle_cells(nd, _ptr(nca), _ptr(pts), n, _ptr(out))
+    return out
+
+
+def expm(As, dT):
+    """Trels for As [..., ndim, ndim+1]."""
+    A = _f32(As)
+    nd = A.shape[-2]
+    out = np.empty_like(A)
+    lib().oracle_expm(nd, _ptr(A), A.size // (nd * (nd + 1)), float(dT), _ptr(out))
+    return out
+
+
+def build_A(basis, theta, ndim):
+    """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T."""
+    th = np.asarray(theta, dtype=np.float64)
+    A = (basis.astype(np.float64) @ th.T).T
+    nC = basis.shape[0] // (ndim * (ndim + 1))
+    return _f32(A.reshape(th.shape[0], nC, ndim, ndim + 1))
+
+
+def project(basis, moments):
+    """dtheta [n_theta, d] = B^T vec(moments)."""
+    m = np.asarray(moments, dtype=np.float64).reshape(moments.shape[0], -1)
+    return _f32((basis.T.astype(np.float64) @ m.T).T)
+
+
+def integrate(nc, points, As, trels, nstepsolver=50, adaptive=False):
+    """Forward integration; points [ndim, nP] or [n_theta, ndim, nP]."""
+    pts, A = _f32(points), _f32(As)
+    nd = A.shape[2]
+    n_theta = A.shape[0]
+    batched = int(pts.ndim == 3)
+    nP = pts.shape[-1]
+    out = np.empty((n_theta, nd, nP), dtype=np.float32)
+    tr = _f32(trels) if trels is not None else None
+    nca = _nc(nc)
+    lib().oracle_forward(nd, _ptr(nca), _ptr(pts), nP, batched, _ptr(tr), _ptr(A), n_theta,
+                         int(nstepsolver), int(adaptive), _ptr(out))
+    return out
+
+
+def midpoint_integrate(nc, points, As, nstepsolver=50, adaptive=False):
+    """The midpoint-rule trajectory end points that the adjoint differentiates."""
+    pts, A = _f32(points), _f32(As)
+    nd, n_theta = A.shape[2], A.shape[0]
+    batched = int(pts.ndim == 3)
+    nP = pts.shape[-1]
+    out = np.empty((n_theta, nd, nP), dtype=np.float32)
+    nca = _nc(nc)
+    lib().oracle_midpoint_forward(nd, _ptr(nca), _ptr(pts), nP, batched, _ptr(A), n_theta,
+                                  int(nstepsolver), int(adaptive), _ptr(out))
+    return out
+
+
+def adjoint(nc, points, As, grad_out, nstepsolver=50, adaptive=False, want_points=True):
+    """Fused adjoint: (moments [n_theta, nC, ppc], grad_points [n_theta, ndim, nP])."""
+    pts, A, g = _f32(points), _f32(As), _f32(grad_out)
+    n_theta, nC, nd = A.shape[0], A.shape[1], A.shape[2]
+    batched = int(pts.ndim == 3)
+    nP = pts.shape[-1]
+    mom = np.empty((n_theta, nC, nd * (nd + 1)), dtype=np.float32)
+    gp = np.empty((n_theta, nd, nP), dtype=np.float32) if want_points else None
+    nca = _nc(nc)
+    lib().oracle_backward(nd, _ptr(nca), _ptr(pts), nP, batched, _ptr(A), n_theta, _ptr(g),
+                          int(nstepsolver), int(adaptive), _ptr(mom), _ptr(gp))
+    return mom, gp
+
+
+def transform(nc, basis, points, theta, nstepsolver=50, adaptive=False):
+    """The reference's forward composition: (x_t, As, Trels)."""
+    nd = len(nc)
+    As = build_A(basis, theta, nd)
+    trels = expm(As, 1.0 / nstepsolver) if nd > 1 else None
+    return integrate(nc, points, As, trels, nstepsolver, adaptive), As, trels
+
+
+def gradient(nc, basis, points, As, grad_out, nstepsolver=50, adaptive=False):
+    """The reference's backward composition: (dtheta, grad_points as returned)."""
+    mom, gp = adjoint(nc, points, As, grad_out, nstepsolver, adaptive, True)
+    if np.asarray(points).ndim == 2:
+        gp = gp.sum(axis=0, dtype=np.float32)
+    return project(basis, mom), gp
+
+
+# ---------------------------------------------------------------------------
+# Resampling (cpab/pytorch/interpolation.py:8-160), float32, op by op.
+# ---------------------------------------------------------------------------
+
+def _axis(g, n):
+    x = (g.astype(np.float32) * np.float32(n - 1)).astype(np.float32)
+    f = np.floor(x)
+    lo = np.clip(f, 0, n - 1)
+    hi = np.clip(f + 1, 0, n - 1)
+    w = (x - lo).astype(np.float32)
+    return lo.astype(np.int64), hi.astype(np.int64), w
+
+
+def _lerp(a, b, w):
+    one = np.float32(1.0)
+    return (a * (one - w)).astype(np.float32) + (b * w).astype(np.float32)
+
+
+def interpolate(ndim, data, grid, outsize):
+    """data [B, C, *in], grid [B, ndim, P] -> [B, C, *outsize]."""
+    data = _f32(data)
+    grid = _f32(grid)
+    B, C = data.shape[:2]
+    bidx = np.arange(B)[:, None]
+    if ndim == 1:
+        x0, x1, xw = _axis(grid[:, 0], data.shape[2])
+        c0 = data[bidx, :, x0]      # [B, P, C]
+        c1 = data[bidx, :, x1]
+        out = _lerp(c0, c1, xw[..., None])
+        return np.ascontiguousarray(out.transpose(0, 2, 1).reshape(B, C, *outsize))
+    if ndim == 2:
+        x0, x1, xw = _axis(grid[:, 0], data.shape[2])
+        y0, y1, yw = _axis(grid[:, 1], data.shape[3])
+        g = lambda xi, yi: data[bidx, :, xi, yi]
+        xw, yw = xw[..., None], yw[..., None]
+        c0 = _lerp(g(x0, y0), g(x1, y0), xw)
+        c1 = _lerp(g(x0, y1), g(x1, y1), xw)
+        c = _lerp(c0, c1, yw)       # [B, P, C], P = i0 + n0*i1
+        n0, n1 = outsize
+        return np.ascontiguousarray(c.reshape(B, n1, n0, C).transpose(0, 3, 2, 1))
+    x0, x1, xw = _axis(grid[:, 0], data.shape[2])
+    y0, y1, yw = _axis(grid[:, 1], data.shape[3])
+    z0, z1, zw = _axis(grid[:, 2], data.shape[4])
+    g = lambda xi, yi, zi: data[bidx, :, xi, yi, zi]
+    xw, yw, zw = xw[..., None], yw[..., None], zw[..., None]
+    c00 = _lerp(g(x0, y0, z0), g(x1, y0, z0), xw)
+    c01 = _lerp(g(x0, y0, z1), g(x1, y0, z1), xw)
+    c10 = _lerp(g(x0, y1, z0), g(x1, y1, z0), xw)
+    c11 = _lerp(g(x0, y1, z1), g(x1, y1, z1), xw)
+    c0 = _lerp(c00, c10, yw)
+    c1 = _lerp(c01, c11, yw)
+    c = _lerp(c0, c1, zw)
+    n0, n1, n2 = outsize
+    return np.ascontiguousarray(c.reshape(B, n2, n1, n0, C).transpose(0, 4, 3, 2, 1))
+
+
+def interpolate_backward(ndim, data, grid, outsize, grad_out):
+    """Gradients (d grid [B, ndim, P], d data [B, C, *in]) of interpolate,
+    accumulated in float64."""
+    data = np.asarray(data, dtype=np.float64)
+    grid = _f32(grid)
+    B, C = data.shape[:2]
+    P = grid.shape[2]
+    g = np.asarray(grad_out, dtype=np.float64)
+    # [B, C, *outsize] -> [B, P, C] with P in grid order (coordinate 0 fastest)
+    g = g.reshape(B, C, -1).transpose(0, 2, 1) if ndim == 1 else np.moveaxis(g, 1, -1).transpose(
+        *([0] + list(range(ndim, 0, -1)) + [ndim + 1])).reshape(B, P, C)
+    dgrid = np.zeros((B, ndim, P))
+    ddata = np.zeros_like(data)
+    bidx = np.arange(B)[:, None]
+    axes = [_axis(grid[:, k], data.shape[2 + k]) for k in range(ndim)]
+    # corner weights per axis: (index, weight, derivative sign)
+    import itertools
+    for corner in itertools.product((0, 1), repeat=ndim):
+        idx, w, dw = [], np.ones((B, P)), []
+        for k, bit in enumerate(corner):
+            lo, hi, wk = axes[k]
+            wk = wk.astype(np.float64)
+            idx.append(hi if bit else lo)
+            w = w * (wk if bit else 1.0 - wk)
+        vals = data[(bidx, slice(None)) + tuple(idx)]          # [B, P, C]
+        gv = (g * vals).sum(-1)                                 # [B, P]
+        for k, bit in enumerate(corner):
+            wk = axes[k][2].astype(np.float64)
+            others = np.ones((B, P))
+            for j, bj in enumerate(corner):
+                if j != k:
+                    wj = axes[j][2].astype(np.float64)
+                    others = others * (wj if bj else 1.0 - wj)
+            dgrid[:, k] += (1.0 if bit else -1.0) * others * gv * (data.shape[2 + k] - 1)
+        contrib = g * w[..., None]                              # [B, P, C]
+        for b in range(B):
+            np.add.at(ddata[b], (slice(None),) + tuple(i[b] for i in idx), contrib[b].T)
+    return dgrid.astype(np.float32), ddata.astype(np.float32)

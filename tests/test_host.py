@@ -1,0 +1,73 @@
+"""Host-side logic that needs no GPU: the Cpab API surface, argument
+checks, grid layout, sharding."""
+import numpy as np
+import pytest
+import torch
+
+from cpab import Cpab
+from cpab.distributed import shard_bounds, shard_points
+from cpab.pytorch.transformer import CPAB_transformer
+from helpers import cpab
+
+
+def test_params_fields_match_reference_layout():
+    T = cpab((20, 20))
+    p = T.params
+    assert (p.ndim, p.nC, p.params_pr_cell, p.D, p.d) == (2, 1600, 6, 9600, 1522)
+    assert p.Ashape == [2, 3] and p.nstepsolver == 50 and p.adaptive_substeps is False
+    assert T.get_theta_dim() == 1522 and T.get_basis() is p.basis
+    assert p.zero_boundary and not p.valid_outside
+    assert "Theta size" in repr(T)
+
+
+def test_constraint_matrix_is_lazy():
+    T = Cpab([3, 3], zero_boundary=False)
+    assert "constrain_mat" not in T.params.__dict__
+    L = T.params.constrain_mat
+    assert L.shape[1] == T.params.D and "constrain_mat" in T.params.__dict__
+
+
+@pytest.mark.parametrize("args", [("20x20",), ([20, 0],), ([2.0, 2],), ([1, 2, 3, 4],)])
+def test_constructor_checks(args):
+    with pytest.raises(AssertionError):
+        Cpab(*args)
+
+
+def test_solver_param_checks():
+    T = cpab((4,))
+    with pytest.raises(AssertionError):
+        T.set_solver_params(0)
+    with pytest.raises(AssertionError):
+        T.set_solver_params(10.0)
+    with pytest.raises(AssertionError):
+        T.set_solver_params(10, adaptive_substeps=1)
+
+
+def test_meshgrid_has_coordinate_zero_fastest():
+    T = cpab((2, 2, 2))
+    g = T.uniform_meshgrid([3, 4, 5], device="cpu")
+    assert g.shape == (3, 60)
+    i0, i1, i2 = 2, 1, 3
+    p = i0 + 3 * (i1 + 4 * i2)
+    np.testing.assert_allclose(g[:, p].numpy(), [i0 / 2, i1 / 3, i2 / 4], rtol=1e-6)
+
+
+def test_cpu_tensors_are_rejected():
+    T = cpab((4, 4))
+    with pytest.raises(AssertionError, match="Only GPU"):
+        CPAB_transformer(torch.zeros(2, 5), torch.zeros(1, T.params.d), T.params)
+
+
+@pytest.mark.parametrize("n,w", [(10, 3), (7, 8), (1000001, 8), (0, 2)])
+def test_shard_bounds_partition(n, w):
+    spans = [shard_bounds(n, r, w) for r in range(w)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    sizes = [hi - lo for lo, hi in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_shard_points_slices_last_axis():
+    x = torch.arange(30.0).reshape(3, 10)
+    parts = [shard_points(x, r, 3) for r in range(3)]
+    assert torch.equal(torch.cat(parts, dim=1), x)
