@@ -18,10 +18,12 @@ _c_int, _c_i64, _c_float, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, cty
 _SIGNATURES = {
     "cpab_b200_expm": [_c_int, _p, _c_i64, _c_float, _p, _p],
     "cpab_b200_build_A": [_c_int, _c_i64, _c_i64, _c_int, _p, _p, _p, _p, _c_float, _p, _p, _p],
-    "cpab_b200_forward": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _c_int, _c_int, _p, _p],
-    "cpab_b200_forward_1d_closed_form": [_p, _c_i64, _c_int, _p, _c_int, _c_int, _p, _p],
-    "cpab_b200_backward": [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _p, _c_int, _c_int, _p, _p,
-                           _p],
+    "cpab_b200_forward": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _p, _c_int, _c_int, _c_int, _p,
+                          _p],
+    "cpab_b200_forward_1d_closed_form": [_p, _c_i64, _c_int, _p, _p, _c_int, _c_int, _p, _p],
+    "cpab_b200_backward": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _p, _c_int, _c_int,
+                           _p, _p, _p],
+    "cpab_b200_order_points": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _p],
     "cpab_b200_cell_index": [_c_int, _p, _p, _c_i64, _p, _p],
     "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],
@@ -122,7 +124,29 @@ def build_A(ndim, nC, basis, theta, dT=None):
     return As, trels
 
 
-def forward(ndim, nc, points, batched, trels, As, nstepsolver, adaptive):
+def order_points(nc, points, batched):
+    """Processing order of the points sorted by initial cell: int32
+    [n_sets, nP] (n_sets = batch when batched, else 1)."""
+    _require(points, "points")
+    nd, nP = points.shape[-2], points.shape[-1]
+    n_sets = points.shape[0] if batched else 1
+    nC = int(np_prod(nc)) * {1: 1, 2: 4, 3: 5}[nd]
+    counts = torch.empty((n_sets, nC), device=points.device, dtype=torch.int32)
+    order = torch.empty((n_sets, nP), device=points.device, dtype=torch.int32)
+    with torch.cuda.device(points.device):
+        _check(lib().cpab_b200_order_points(nd, _i32_array(nc), _ptr(points), nP, n_sets,
+                                            _ptr(counts), _ptr(order), _stream(points.device)))
+    return order
+
+
+def np_prod(xs):
+    r = 1
+    for x in xs:
+        r *= int(x)
+    return r
+
+
+def forward(ndim, nc, points, batched, trels, As, nstepsolver, adaptive, order=None):
     _require(points, "points")
     _require(As, "As")
     n_theta = As.shape[0]
@@ -131,17 +155,19 @@ def forward(ndim, nc, points, batched, trels, As, nstepsolver, adaptive):
     with torch.cuda.device(As.device):
         if ndim == 1:
             _check(lib().cpab_b200_forward_1d_closed_form(
-                _ptr(points), nP, int(batched), _ptr(As), n_theta, int(nc[0]), _ptr(out),
-                _stream(As.device)))
+                _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_theta, int(nc[0]),
+                _ptr(out), _stream(As.device)))
         else:
             _require(trels, "Trels")
             _check(lib().cpab_b200_forward(
-                ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(trels), _ptr(As),
-                n_theta, int(nstepsolver), int(adaptive), _ptr(out), _stream(As.device)))
+                ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(trels),
+                _ptr(As), n_theta, int(nstepsolver), int(adaptive), _ptr(out),
+                _stream(As.device)))
     return out
 
 
-def backward(ndim, nc, points, batched, As, grad_out, nstepsolver, adaptive, want_points):
+def backward(ndim, nc, points, batched, As, grad_out, nstepsolver, adaptive, want_points,
+             order=None):
     """Returns (moments [n_theta, nC, ppc], grad_points [n_theta, ndim, nP] or None)."""
     _require(points, "points")
     _require(As, "As")
@@ -154,7 +180,7 @@ def backward(ndim, nc, points, batched, As, grad_out, nstepsolver, adaptive, wan
           if want_points else None)
     with torch.cuda.device(As.device):
         _check(lib().cpab_b200_backward(
-            ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(As), n_theta,
+            ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_theta,
             _ptr(grad_out), int(nstepsolver), int(adaptive), _ptr(moments), _ptr(gp),
             _stream(As.device)))
     return moments, gp

@@ -1,9 +1,10 @@
 """Differentiable CPA transformation of points (cpab/pytorch/transformer.py of
 the reference), backed by libcpab_b200.
 
-Forward:  A = B theta (+ Trels = expm(A / nstepsolver), fused), then the
-          integration kernel (closed form in 1D, nstepsolver exact per-cell
-          steps in 2D/3D).
+Forward:  A = B theta (+ Trels = expm(A / nstepsolver), fused), a counting
+          sort of the points by initial cell (processing order only), then
+          the integration kernel (closed form in 1D, nstepsolver exact
+          per-cell steps in 2D/3D).
 Backward: the fused adjoint kernel produces per-cell moments (and the point
           gradient lambda(0) when the points need one), then one sparse
           projection dtheta = B^T vec(moments).  Optionally the projected
@@ -94,6 +95,10 @@ def _nc(params):
     return [int(c) for c in params.nc]
 
 
+# Below this many points per set the kernels take the points in storage order.
+ORDER_MIN_POINTS = 4096
+
+
 class _CPABFunction(torch.autograd.Function):
     """A = B theta -> integrate; backward: fused adjoint moments -> B^T projection."""
 
@@ -108,13 +113,16 @@ class _CPABFunction(torch.autograd.Function):
         adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
         dT = None if nd == 1 else 1.0 / T
         As, trels = _native.build_A(nd, int(params.nC), basis, theta_c, dT)
-        out = _native.forward(nd, _nc(params), points_c, batched, trels, As, T, adaptive)
+        order = (_native.order_points(_nc(params), points_c, batched)
+                 if points_c.shape[-1] >= ORDER_MIN_POINTS else None)
+        out = _native.forward(nd, _nc(params), points_c, batched, trels, As, T, adaptive, order)
         ctx.params = params
         ctx.batched = batched
         ctx.nstepsolver = T
         ctx.adaptive = adaptive
         ctx.compute_points_grad = compute_points_grad
         ctx.group = group
+        ctx.order = order
         ctx.save_for_backward(points_c, As)
         return out
 
@@ -126,7 +134,7 @@ class _CPABFunction(torch.autograd.Function):
         want_points = ctx.compute_points_grad and ctx.needs_input_grad[0]
         moments, grad_points = _native.backward(
             params.ndim, _nc(params), points, ctx.batched, As, grad.contiguous(),
-            ctx.nstepsolver, ctx.adaptive, want_points)
+            ctx.nstepsolver, ctx.adaptive, want_points, ctx.order)
         if grad_points is not None and points.dim() == 2:
             grad_points = grad_points.sum(dim=0)
         grad_theta = None

@@ -21,69 +21,91 @@ namespace {
 //   R = (I - M/2 + M^2/12)^-1 (I + M/2 + M^2/12),
 // the scheme of cpab/core/cpab_ops_2d.cu:585-701 (2D) and
 // cpab/core/cpab_ops_3d.cu:538-674 (3D); the 1D case is the closed form of
-// cpab/core/cpab_ops_1d.cu:442-467.  The operation order follows those
-// kernels so Trels agree to the last bits.
+// cpab/core/cpab_ops_1d.cu:442-467.
+//
+// Every sum of products is evaluated left to right with the first two
+// products fused as fma(a, b, c*d) and each further product fused onto the
+// running sum -- the rounding the reference's kernels get from the compiler,
+// written out explicitly so that the result does not depend on contraction
+// heuristics.  (Checked bit for bit against Trels computed by the
+// reference's own kernels on a B200.)
 // ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float dot2(float a, float b, float c, float d) {
+  return __fmaf_rn(a, b, __fmul_rn(c, d));
+}
+__device__ __forceinline__ float dot3(float a, float b, float c, float d, float e, float f) {
+  return __fmaf_rn(e, f, __fmaf_rn(a, b, __fmul_rn(c, d)));
+}
+__device__ __forceinline__ float diff2(float a, float b, float c, float d) {
+  return __fmaf_rn(a, b, -__fmul_rn(c, d));
+}
+// 1 + h m + s q, h m + s q  (Pade numerator/denominator entries)
+__device__ __forceinline__ float pade_diag(float h, float m, float s, float q) {
+  return __fmaf_rn(s, q, __fmaf_rn(h, m, 1.0f));
+}
+__device__ __forceinline__ float pade_off(float h, float m, float s, float q) {
+  return __fmaf_rn(h, m, __fmul_rn(s, q));
+}
 
 __device__ __forceinline__ int squarings(float norm) {
   return norm > 0.5f ? (int)ceilf(log2f(norm * 2.0f)) : 0;
 }
 
 __device__ __forceinline__ void expm1d(const float (&a)[2], float dT, float (&r)[2]) {
-  const float m0 = dT * a[0];
-  const float m1 = dT * a[1];
+  const float m0 = __fmul_rn(dT, a[0]);
+  const float m1 = __fmul_rn(dT, a[1]);
   float rel;  // (e^m0 - 1) / m0
   if (fabsf(m0) > 1e-6f) {
     rel = expm1f(m0) / m0;
   } else {
-    const float sq = m0 * m0;
-    rel = 1.0f + 0.5f * m0 + (1.0f / 6.0f) * sq + (1.0f / 24.0f) * sq * m0;
+    const float sq = __fmul_rn(m0, m0);
+    rel = __fmaf_rn(__fmul_rn(1.0f / 24.0f, sq), m0,
+                    __fmaf_rn(1.0f / 6.0f, sq, __fmaf_rn(0.5f, m0, 1.0f)));
   }
   r[0] = expf(m0);
-  r[1] = m1 * rel;
+  r[1] = __fmul_rn(m1, rel);
 }
 
 __device__ __forceinline__ void expm2d(const float (&a)[6], float dT, float (&r)[6]) {
   float m[6];
 #pragma unroll
-  for (int k = 0; k < 6; ++k) m[k] = dT * a[k];
-  const float nrm = sqrtf(m[0] * m[0] + m[1] * m[1] + m[2] * m[2] + m[3] * m[3] +
-                          m[4] * m[4] + m[5] * m[5]);
-  const int ns = squarings(nrm);
+  for (int k = 0; k < 6; ++k) m[k] = __fmul_rn(dT, a[k]);
+  float sq = dot2(m[0], m[0], m[1], m[1]);
+#pragma unroll
+  for (int k = 2; k < 6; ++k) sq = __fmaf_rn(m[k], m[k], sq);
+  const int ns = squarings(sqrtf(sq));
   float sc = 1.0f;
   for (int i = 0; i < ns; ++i) sc *= 0.5f;
 #pragma unroll
-  for (int k = 0; k < 6; ++k) m[k] *= sc;
+  for (int k = 0; k < 6; ++k) m[k] = __fmul_rn(m[k], sc);
   // Rows of M^2 (the third row of M is zero).
-  const float s00 = m[0] * m[0] + m[1] * m[3];
-  const float s01 = m[0] * m[1] + m[1] * m[4];
-  const float s02 = m[0] * m[2] + m[1] * m[5];
-  const float s10 = m[3] * m[0] + m[4] * m[3];
-  const float s11 = m[3] * m[1] + m[4] * m[4];
-  const float s12 = m[3] * m[2] + m[4] * m[5];
+  const float s00 = dot2(m[0], m[0], m[1], m[3]), s01 = dot2(m[0], m[1], m[1], m[4]);
+  const float s02 = dot2(m[0], m[2], m[1], m[5]), s10 = dot2(m[3], m[0], m[4], m[3]);
+  const float s11 = dot2(m[3], m[1], m[4], m[4]), s12 = dot2(m[3], m[2], m[4], m[5]);
   const float c12 = 1.0f / 12.0f;
   // Numerator N = I + M/2 + M^2/12, denominator D = I - M/2 + M^2/12.
-  const float n00 = 1.0f + 0.5f * m[0] + c12 * s00, d00 = 1.0f - 0.5f * m[0] + c12 * s00;
-  const float n01 = 0.5f * m[1] + c12 * s01, d01 = -0.5f * m[1] + c12 * s01;
-  const float n02 = 0.5f * m[2] + c12 * s02, d02 = -0.5f * m[2] + c12 * s02;
-  const float n10 = 0.5f * m[3] + c12 * s10, d10 = -0.5f * m[3] + c12 * s10;
-  const float n11 = 1.0f + 0.5f * m[4] + c12 * s11, d11 = 1.0f - 0.5f * m[4] + c12 * s11;
-  const float n12 = 0.5f * m[5] + c12 * s12, d12 = -0.5f * m[5] + c12 * s12;
+  const float n00 = pade_diag(0.5f, m[0], c12, s00), d00 = pade_diag(-0.5f, m[0], c12, s00);
+  const float n01 = pade_off(0.5f, m[1], c12, s01), d01 = pade_off(-0.5f, m[1], c12, s01);
+  const float n02 = pade_off(0.5f, m[2], c12, s02), d02 = pade_off(-0.5f, m[2], c12, s02);
+  const float n10 = pade_off(0.5f, m[3], c12, s10), d10 = pade_off(-0.5f, m[3], c12, s10);
+  const float n11 = pade_diag(0.5f, m[4], c12, s11), d11 = pade_diag(-0.5f, m[4], c12, s11);
+  const float n12 = pade_off(0.5f, m[5], c12, s12), d12 = pade_off(-0.5f, m[5], c12, s12);
   // D^-1 = [Di, -Di d_t; 0 1] with Di the inverse of D's 2x2 linear block.
-  const float idet = 1.0f / (d00 * d11 - d01 * d10);
-  const float i00 = d11 * idet, i01 = -d01 * idet;
-  const float i10 = -d10 * idet, i11 = d00 * idet;
-  const float i02 = -(i00 * d02 + i01 * d12);
-  const float i12 = -(i10 * d02 + i11 * d12);
-  float r00 = i00 * n00 + i01 * n10, r01 = i00 * n01 + i01 * n11;
-  float r02 = i00 * n02 + i01 * n12 + i02;
-  float r10 = i10 * n00 + i11 * n10, r11 = i10 * n01 + i11 * n11;
-  float r12 = i10 * n02 + i11 * n12 + i12;
+  const float idet = 1.0f / diff2(d00, d11, d01, d10);
+  const float i00 = __fmul_rn(d11, idet), i01 = __fmul_rn(-d01, idet);
+  const float i10 = __fmul_rn(-d10, idet), i11 = __fmul_rn(d00, idet);
+  const float i02 = -dot2(i00, d02, i01, d12);
+  const float i12 = -dot2(i10, d02, i11, d12);
+  float r00 = dot2(i00, n00, i01, n10), r01 = dot2(i00, n01, i01, n11);
+  float r02 = __fadd_rn(dot2(i00, n02, i01, n12), i02);
+  float r10 = dot2(i10, n00, i11, n10), r11 = dot2(i10, n01, i11, n11);
+  float r12 = __fadd_rn(dot2(i10, n02, i11, n12), i12);
   for (int i = 0; i < ns; ++i) {
-    const float t00 = r00 * r00 + r01 * r10, t01 = r00 * r01 + r01 * r11;
-    const float t02 = r00 * r02 + r01 * r12 + r02;
-    const float t10 = r10 * r00 + r11 * r10, t11 = r10 * r01 + r11 * r11;
-    const float t12 = r10 * r02 + r11 * r12 + r12;
+    const float t00 = dot2(r00, r00, r01, r10), t01 = dot2(r00, r01, r01, r11);
+    const float t02 = __fadd_rn(dot2(r00, r02, r01, r12), r02);
+    const float t10 = dot2(r10, r00, r11, r10), t11 = dot2(r10, r01, r11, r11);
+    const float t12 = __fadd_rn(dot2(r10, r02, r11, r12), r12);
     r00 = t00; r01 = t01; r02 = t02; r10 = t10; r11 = t11; r12 = t12;
   }
   r[0] = r00; r[1] = r01; r[2] = r02; r[3] = r10; r[4] = r11; r[5] = r12;
@@ -95,27 +117,35 @@ __device__ __forceinline__ void expm3d(const float (&a)[12], float dT, float (&r
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) L[i][j] = dT * a[i * 4 + j];
-    u[i] = dT * a[i * 4 + 3];
+    for (int j = 0; j < 3; ++j) L[i][j] = __fmul_rn(dT, a[i * 4 + j]);
+    u[i] = __fmul_rn(dT, a[i * 4 + 3]);
   }
-  const float nrm = sqrtf(L[0][0] * L[0][0] + L[0][1] * L[0][1] + L[0][2] * L[0][2] + u[0] * u[0] +
-                          L[1][0] * L[1][0] + L[1][1] * L[1][1] + L[1][2] * L[1][2] + u[1] * u[1] +
-                          L[2][0] * L[2][0] + L[2][1] * L[2][1] + L[2][2] * L[2][2] + u[2] * u[2]);
-  const int ns = squarings(nrm);
+  // Squared Frobenius norm in row-major order (translation last in each row).
+  float sq = dot2(L[0][0], L[0][0], L[0][1], L[0][1]);
+  sq = __fmaf_rn(L[0][2], L[0][2], sq);
+  sq = __fmaf_rn(u[0], u[0], sq);
+#pragma unroll
+  for (int i = 1; i < 3; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) sq = __fmaf_rn(L[i][j], L[i][j], sq);
+    sq = __fmaf_rn(u[i], u[i], sq);
+  }
+  const int ns = squarings(sqrtf(sq));
   float sc = 1.0f;
   for (int i = 0; i < ns; ++i) sc *= 0.5f;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) L[i][j] *= sc;
-    u[i] *= sc;
+    for (int j = 0; j < 3; ++j) L[i][j] = __fmul_rn(L[i][j], sc);
+    u[i] = __fmul_rn(u[i], sc);
   }
   float S[3][3], su[3];  // M^2: linear block L*L and translation L*u
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) S[i][j] = L[i][0] * L[0][j] + L[i][1] * L[1][j] + L[i][2] * L[2][j];
-    su[i] = L[i][0] * u[0] + L[i][1] * u[1] + L[i][2] * u[2];
+    for (int j = 0; j < 3; ++j)
+      S[i][j] = dot3(L[i][0], L[0][j], L[i][1], L[1][j], L[i][2], L[2][j]);
+    su[i] = dot3(L[i][0], u[0], L[i][1], u[1], L[i][2], u[2]);
   }
   const float c12 = 1.0f / 12.0f;
   float N[3][3], D[3][3], nu[3], du[3];
@@ -123,45 +153,44 @@ __device__ __forceinline__ void expm3d(const float (&a)[12], float dT, float (&r
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      const float id = (i == j) ? 1.0f : 0.0f;
-      N[i][j] = (i == j) ? id + 0.5f * L[i][j] + c12 * S[i][j] : 0.5f * L[i][j] + c12 * S[i][j];
-      D[i][j] = (i == j) ? id - 0.5f * L[i][j] + c12 * S[i][j] : -0.5f * L[i][j] + c12 * S[i][j];
+      N[i][j] = i == j ? pade_diag(0.5f, L[i][j], c12, S[i][j]) : pade_off(0.5f, L[i][j], c12, S[i][j]);
+      D[i][j] = i == j ? pade_diag(-0.5f, L[i][j], c12, S[i][j]) : pade_off(-0.5f, L[i][j], c12, S[i][j]);
     }
-    nu[i] = 0.5f * u[i] + c12 * su[i];
-    du[i] = -0.5f * u[i] + c12 * su[i];
+    nu[i] = pade_off(0.5f, u[i], c12, su[i]);
+    du[i] = pade_off(-0.5f, u[i], c12, su[i]);
   }
   // Inverse of D's linear block by cofactors.
-  const float det = D[0][0] * (D[1][1] * D[2][2] - D[1][2] * D[2][1]) -
-                    D[0][1] * (D[1][0] * D[2][2] - D[1][2] * D[2][0]) +
-                    D[0][2] * (D[1][0] * D[2][1] - D[1][1] * D[2][0]);
-  const float id = 1.0f / det;
+  const float c0 = diff2(D[1][1], D[2][2], D[1][2], D[2][1]);
+  const float c1 = diff2(D[1][0], D[2][2], D[1][2], D[2][0]);
+  const float c2 = diff2(D[1][0], D[2][1], D[1][1], D[2][0]);
+  const float id = 1.0f / __fmaf_rn(D[0][2], c2, __fmaf_rn(D[0][0], c0, -__fmul_rn(D[0][1], c1)));
   float I[3][3];
-  I[0][0] = (D[1][1] * D[2][2] - D[1][2] * D[2][1]) * id;
-  I[0][1] = (D[0][2] * D[2][1] - D[0][1] * D[2][2]) * id;
-  I[0][2] = (D[0][1] * D[1][2] - D[0][2] * D[1][1]) * id;
-  I[1][0] = (D[1][2] * D[2][0] - D[1][0] * D[2][2]) * id;
-  I[1][1] = (D[0][0] * D[2][2] - D[0][2] * D[2][0]) * id;
-  I[1][2] = (D[0][2] * D[1][0] - D[0][0] * D[1][2]) * id;
-  I[2][0] = (D[1][0] * D[2][1] - D[1][1] * D[2][0]) * id;
-  I[2][1] = (D[0][1] * D[2][0] - D[0][0] * D[2][1]) * id;
-  I[2][2] = (D[0][0] * D[1][1] - D[0][1] * D[1][0]) * id;
-  float it[3];
-#pragma unroll
-  for (int i = 0; i < 3; ++i) it[i] = -(I[i][0] * du[0] + I[i][1] * du[1] + I[i][2] * du[2]);
+  I[0][0] = __fmul_rn(c0, id);
+  I[0][1] = __fmul_rn(diff2(D[0][2], D[2][1], D[0][1], D[2][2]), id);
+  I[0][2] = __fmul_rn(diff2(D[0][1], D[1][2], D[0][2], D[1][1]), id);
+  I[1][0] = __fmul_rn(diff2(D[1][2], D[2][0], D[1][0], D[2][2]), id);
+  I[1][1] = __fmul_rn(diff2(D[0][0], D[2][2], D[0][2], D[2][0]), id);
+  I[1][2] = __fmul_rn(diff2(D[0][2], D[1][0], D[0][0], D[1][2]), id);
+  I[2][0] = __fmul_rn(c2, id);
+  I[2][1] = __fmul_rn(diff2(D[0][1], D[2][0], D[0][0], D[2][1]), id);
+  I[2][2] = __fmul_rn(diff2(D[0][0], D[1][1], D[0][1], D[1][0]), id);
   float R[3][3], ru[3];
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
+    const float it = -dot3(I[i][0], du[0], I[i][1], du[1], I[i][2], du[2]);
 #pragma unroll
-    for (int j = 0; j < 3; ++j) R[i][j] = I[i][0] * N[0][j] + I[i][1] * N[1][j] + I[i][2] * N[2][j];
-    ru[i] = I[i][0] * nu[0] + I[i][1] * nu[1] + I[i][2] * nu[2] + it[i];
+    for (int j = 0; j < 3; ++j)
+      R[i][j] = dot3(I[i][0], N[0][j], I[i][1], N[1][j], I[i][2], N[2][j]);
+    ru[i] = __fadd_rn(dot3(I[i][0], nu[0], I[i][1], nu[1], I[i][2], nu[2]), it);
   }
   for (int s = 0; s < ns; ++s) {
     float Q[3][3], qu[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
 #pragma unroll
-      for (int j = 0; j < 3; ++j) Q[i][j] = R[i][0] * R[0][j] + R[i][1] * R[1][j] + R[i][2] * R[2][j];
-      qu[i] = R[i][0] * ru[0] + R[i][1] * ru[1] + R[i][2] * ru[2] + ru[i];
+      for (int j = 0; j < 3; ++j)
+        Q[i][j] = dot3(R[i][0], R[0][j], R[i][1], R[1][j], R[i][2], R[2][j]);
+      qu[i] = __fadd_rn(dot3(R[i][0], ru[0], R[i][1], ru[1], R[i][2], ru[2]), ru[i]);
     }
 #pragma unroll
     for (int i = 0; i < 3; ++i) {

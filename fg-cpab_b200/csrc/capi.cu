@@ -136,8 +136,8 @@ int cpab_b200_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_
 }
 
 int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP, int points_batched,
-                                     const float *As, int n_theta, int ncx, float *out,
-                                     cpab_stream_t stream) {
+                                     const int32_t *order, const float *As, int n_theta, int ncx,
+                                     float *out, cpab_stream_t stream) {
   cpab::IntegrateArgs a;
   const int32_t nc[1] = {ncx};
   int st = check_integrate("forward_1d_closed_form", 1, nc, points, nP, points_batched, As, n_theta,
@@ -146,11 +146,13 @@ int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP, int points
   if (nP == 0 || n_theta == 0) return ok();
   if (out == nullptr) return fail(CPAB_ERR_ARG, "forward_1d_closed_form: null output");
   a.out = out;
+  a.order = order;
   return cuda_status(cpab::launch_forward_1d(a, stream), "forward_1d_closed_form");
 }
 
 int cpab_b200_forward(int ndim, const int32_t *nc, const float *points, int64_t nP,
-                      int points_batched, const float *trels, const float *As, int n_theta,
+                      int points_batched, const int32_t *order, const float *trels,
+                      const float *As, int n_theta,
                       int nstepsolver, int adaptive, float *out, cpab_stream_t stream) {
   cpab::IntegrateArgs a;
   int st = check_integrate("forward", ndim, nc, points, nP, points_batched, As, n_theta,
@@ -162,11 +164,13 @@ int cpab_b200_forward(int ndim, const int32_t *nc, const float *points, int64_t 
   if (!aligned16(trels)) return fail(CPAB_ERR_ARG, "forward: trels must be 16-byte aligned");
   a.trels = trels;
   a.out = out;
+  a.order = order;
   return cuda_status(cpab::launch_forward(a, stream), "forward");
 }
 
 int cpab_b200_backward(int ndim, const int32_t *nc, const float *points, int64_t nP,
-                       int points_batched, const float *As, int n_theta, const float *grad_out,
+                       int points_batched, const int32_t *order, const float *As, int n_theta,
+                       const float *grad_out,
                        int nstepsolver, int adaptive, float *moments, float *grad_points,
                        cpab_stream_t stream) {
   cpab::IntegrateArgs a;
@@ -183,7 +187,24 @@ int cpab_b200_backward(int ndim, const int32_t *nc, const float *points, int64_t
   a.grad_out = grad_out;
   a.moments = moments;
   a.grad_points = grad_points;
+  a.order = order;
   return cuda_status(cpab::launch_backward(a, stream), "backward");
+}
+
+int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points, int64_t nP,
+                           int n_sets, int32_t *counts_scratch, int32_t *order,
+                           cpab_stream_t stream) {
+  if (ndim < 1 || ndim > 3) return fail(CPAB_ERR_ARG, "order_points: ndim must be 1, 2 or 3");
+  const int64_t nC = cell_count(ndim, nc);
+  if (nC <= 0) return fail(CPAB_ERR_ARG, "order_points: tessellation sizes must be in [1, 2^20]");
+  if (nP < 0 || n_sets < 0) return fail(CPAB_ERR_ARG, "order_points: negative size");
+  if (n_sets > 65535) return fail(CPAB_ERR_SIZE, "order_points: more than 65535 point sets");
+  if (nP > INT32_MAX) return fail(CPAB_ERR_SIZE, "order_points: more than 2^31-1 points");
+  if (nP > 0 && n_sets > 0 && (points == nullptr || counts_scratch == nullptr || order == nullptr))
+    return fail(CPAB_ERR_ARG, "order_points: null pointer");
+  return cuda_status(cpab::launch_order_points(ndim, make_tess(ndim, nc), points, nP, n_sets,
+                                               (int)nC, counts_scratch, order, stream),
+                     "order_points");
 }
 
 int cpab_b200_cell_index(int ndim, const int32_t *nc, const float *points, int64_t n,

@@ -25,8 +25,7 @@ constexpr int kMaxSegs = kMaxSteps / kSegSteps;
 constexpr float kOneMinusEps = 1.0f - 1e-7f;
 
 template <int ND> struct Dim {
-  static constexpr int kPpc = ND * (ND + 1);               // params per cell
-  static constexpr int kStride = ND == 1 ? 2 : (ND == 2 ? 8 : 12);  // smem floats per cell
+  static constexpr int kPpc = ND * (ND + 1);  // params per cell (= row length of a cell table)
 };
 
 // Tessellation geometry passed by value to kernels.
@@ -58,13 +57,14 @@ __device__ __forceinline__ int cell_of(const Tess &t, float x) {
 
 // 2D: four triangles per square numbered bottom(0) right(1) top(2) left(3);
 // outside the unit square the triangle facing the nearest boundary part is
-// used.  cpab/core/cpab_ops_2d.cu:71-128 (the reference's `a*b - c`
+// used.  cpab/core/cpab_ops_2d.cu:119-176 (the reference's `a*b - c`
 // comparisons are contracted to fma by nvcc; they are written as fmaf here).
-__device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
+// Points strictly inside the square take a short path: there the reference's
+// lower clamp is the identity and none of its boundary branches is taken.
+static __device__ __noinline__ int cell_of_2d_outside(const Tess &t, float px, float py) {
   const float xc = fminf(fmaxf(px, 0.0f), kOneMinusEps);
   const float yc = fminf(fmaxf(py, 0.0f), kOneMinusEps);
   int ix, iy;
-  // xc * n < n for every n < 2^24 because xc <= 1 - 2^-23: no upper clamp.
   const float fx0 = floor_nonneg(xc * t.fx, ix);
   const float fy0 = floor_nonneg(yc * t.fy, iy);
   const int base = (ix + iy * t.nx) << 2;
@@ -80,32 +80,32 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
   }
   if (py <= 0.0f) return base;
   if (py >= 1.0f) return base + 2;
+  // Unreachable for finite inputs (handled by the caller's inside path) but
+  // kept for NaN coordinates, which fail every comparison above.
+  const float lx = fmaf(xc, t.fx, -fx0);
+  const float ly = fmaf(yc, t.fy, -fy0);
+  return base + (((lx < ly) * 3) ^ ((1.0f - lx) < ly));
+}
+
+__device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
+  if (!(px > 0.0f && px < 1.0f && py > 0.0f && py < 1.0f)) return cell_of_2d_outside(t, px, py);
+  const float xc = fminf(px, kOneMinusEps);
+  const float yc = fminf(py, kOneMinusEps);
+  int ix, iy;
+  // xc * n < n for every n < 2^24 because xc <= 1 - 2^-23: no upper clamp.
+  const float fx0 = floor_nonneg(xc * t.fx, ix);
+  const float fy0 = floor_nonneg(yc * t.fy, iy);
   const float lx = fmaf(xc, t.fx, -fx0);
   const float ly = fmaf(yc, t.fy, -fy0);
   const int upper_left = lx < ly;           // above the main diagonal
   const int upper_right = (1.0f - lx) < ly;  // above the anti-diagonal
-  return base + ((upper_left * 3) ^ upper_right);
+  return ((ix + iy * t.nx) << 2) + ((upper_left * 3) ^ upper_right);
 }
 
 // 3D: five tetrahedra per cube (central one = 0), cube parity flips the
 // split; beyond a corner the coordinate with the smallest overshoot is moved
 // half a cell inside.  cpab/core/cpab_ops_3d.cu:67-131.
-__device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
-  const float ox = (fabsf(px - 0.5f) - 0.5f) * t.fx;
-  const float oy = (fabsf(py - 0.5f) - 0.5f) * t.fy;
-  const float oz = (fabsf(pz - 0.5f) - 0.5f) * t.fz;
-  if (ox > 0.0f && oy > 0.0f && oz > 0.0f) {
-    if (ox <= oy && ox <= oz) {
-      px = (px < 0.5f) ? t.hx : 1.0f - t.hx;
-    } else if (oy <= oz) {
-      py = (py < 0.5f) ? t.hy : 1.0f - t.hy;
-    } else {
-      pz = (pz < 0.5f) ? t.hz : 1.0f - t.hz;
-    }
-  }
-  const float sx = fminf(fmaxf(px, 0.0f), 1.0f) * t.fx;
-  const float sy = fminf(fmaxf(py, 0.0f), 1.0f) * t.fy;
-  const float sz = fminf(fmaxf(pz, 0.0f), 1.0f) * t.fz;
+__device__ __forceinline__ int tet_in_cube(const Tess &t, float sx, float sy, float sz) {
   int i, j, k;
   float fi = floor_nonneg(sx, i);
   float fj = floor_nonneg(sy, j);
@@ -117,7 +117,7 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float 
   float x = sx - fi;
   float y = sy - fj;
   const float z = sz - fk;
-  int c = 5 * (i + t.nx * (j + t.ny * k));
+  const int c = 5 * (i + t.nx * (j + t.ny * k));
   if ((i ^ j ^ k) & 1) {  // odd cubes: rotate the local frame by 90 degrees
     const float x0 = x;
     x = y;
@@ -130,9 +130,36 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float 
   return c;
 }
 
+static __device__ __noinline__ int cell_of_3d_outside(const Tess &t, float px, float py, float pz) {
+  const float ox = (fabsf(px - 0.5f) - 0.5f) * t.fx;
+  const float oy = (fabsf(py - 0.5f) - 0.5f) * t.fy;
+  const float oz = (fabsf(pz - 0.5f) - 0.5f) * t.fz;
+  if (ox > 0.0f && oy > 0.0f && oz > 0.0f) {
+    if (ox <= oy && ox <= oz) {
+      px = (px < 0.5f) ? t.hx : 1.0f - t.hx;
+    } else if (oy <= oz) {
+      py = (py < 0.5f) ? t.hy : 1.0f - t.hy;
+    } else {
+      pz = (pz < 0.5f) ? t.hz : 1.0f - t.hz;
+    }
+  }
+  return tet_in_cube(t, fminf(fmaxf(px, 0.0f), 1.0f) * t.fx, fminf(fmaxf(py, 0.0f), 1.0f) * t.fy,
+                     fminf(fmaxf(pz, 0.0f), 1.0f) * t.fz);
+}
+
+__device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
+  // Inside the closed unit cube the clamps are identities and the corner rule
+  // does not apply.
+  if (px >= 0.0f && px <= 1.0f && py >= 0.0f && py <= 1.0f && pz >= 0.0f && pz <= 1.0f)
+    return tet_in_cube(t, px * t.fx, py * t.fy, pz * t.fz);
+  return cell_of_3d_outside(t, px, py, pz);
+}
+
 // ---------------------------------------------------------------------------
-// Cell tables.  A table holds kPpc floats per cell; in shared memory each
-// cell is padded to Dim<ND>::kStride floats so it loads with 128-bit LDS.
+// Cell tables: kPpc floats per cell, rows packed back to back (the layout of
+// the reference's As/Trels).  A 2D row is 24 bytes and loads as three 64-bit
+// words; a 3D row is 48 bytes, three 128-bit words.  Packed rows spread
+// neighbouring cells over distinct shared-memory banks.
 // ---------------------------------------------------------------------------
 
 template <int ND, bool SMEM>
@@ -143,16 +170,10 @@ __device__ __forceinline__ void load_cell(const float *__restrict__ tab, int c,
                           : __ldg(reinterpret_cast<const float2 *>(tab) + c);
     m[0] = v.x; m[1] = v.y;
   } else if constexpr (ND == 2) {
-    if constexpr (SMEM) {
-      const float4 *p = reinterpret_cast<const float4 *>(tab) + 2 * c;
-      const float4 u = p[0];
-      const float2 w = *reinterpret_cast<const float2 *>(p + 1);
-      m[0] = u.x; m[1] = u.y; m[2] = u.z; m[3] = u.w; m[4] = w.x; m[5] = w.y;
-    } else {
-      const float2 *p = reinterpret_cast<const float2 *>(tab) + 3 * c;
-      const float2 u = __ldg(p), v = __ldg(p + 1), w = __ldg(p + 2);
-      m[0] = u.x; m[1] = u.y; m[2] = v.x; m[3] = v.y; m[4] = w.x; m[5] = w.y;
-    }
+    const float2 *p = reinterpret_cast<const float2 *>(tab) + 3 * c;
+    const float2 u = SMEM ? p[0] : __ldg(p), v = SMEM ? p[1] : __ldg(p + 1),
+                 w = SMEM ? p[2] : __ldg(p + 2);
+    m[0] = u.x; m[1] = u.y; m[2] = v.x; m[3] = v.y; m[4] = w.x; m[5] = w.y;
   } else {
     const float4 *p = reinterpret_cast<const float4 *>(tab) + 3 * c;
     const float4 u = SMEM ? p[0] : __ldg(p);
@@ -164,16 +185,12 @@ __device__ __forceinline__ void load_cell(const float *__restrict__ tab, int c,
   }
 }
 
-// Copy nC cells of kPpc floats from global memory into a padded smem table.
-template <int ND>
+// Copy n floats (a multiple of 2, 8-byte aligned) from global to shared memory.
 __device__ __forceinline__ void stage_table(float *__restrict__ s, const float *__restrict__ g,
-                                            int nC) {
-  constexpr int P = Dim<ND>::kPpc, S = Dim<ND>::kStride;
-  const int n = nC * P;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int c = i / P;
-    s[c * S + (i - c * P)] = __ldg(g + i);
-  }
+                                            int n) {
+  const float2 *g2 = reinterpret_cast<const float2 *>(g);
+  float2 *s2 = reinterpret_cast<float2 *>(s);
+  for (int i = threadIdx.x; i < n / 2; i += blockDim.x) s2[i] = __ldg(g2 + i);
 }
 
 // ---------------------------------------------------------------------------

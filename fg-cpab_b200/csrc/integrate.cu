@@ -24,11 +24,17 @@ namespace cpab {
 
 namespace {
 
-constexpr int kFwdThreads = 256;
-constexpr int kBwdThreads = 256;
-// Shared-memory budget per block; two blocks per SM keep 16+ warps resident.
+constexpr int kFwdThreads = 512;
+constexpr int kBwdThreads = 512;
+// Shared-memory budget per block (cell table, plus the moment table in the
+// backward): two 512-thread blocks per SM give 32 resident warps.
 constexpr size_t kFwdSmemBudget = 100 * 1024;
 constexpr size_t kBwdSmemBudget = 110 * 1024;
+
+// Point processed by thread slot i: order[set][i] when an order is given.
+__device__ __forceinline__ int64_t point_of(const int32_t *__restrict__ order, int64_t i) {
+  return order ? (int64_t)__ldg(order + i) : i;
+}
 
 // ---------------------------------------------------------------------------
 // 1D closed form.  cpab/core/cpab_ops_1d.cu:103-205.
@@ -79,10 +85,12 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_1d(IntegrateArgs a) {
   const float2 *tab = reinterpret_cast<const float2 *>(SMEM ? s_tab : ag);
   const float *pin = a.points + (a.batched ? (int64_t)b * a.nP : 0);
   float *pout = a.out + (int64_t)b * a.nP;
+  const int32_t *ord = a.order ? a.order + (a.batched ? (int64_t)b * a.nP : 0) : nullptr;
   const Tess t = a.tess;
   const int nx = t.nx;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < a.nP;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < a.nP;
+       slot += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = point_of(ord, slot);
     float x = __ldg(pin + i);
     float tr = 1.0f;
     int c = cell_of(t, x);
@@ -125,7 +133,7 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
   const float *tg = a.trels + (int64_t)b * a.nC * P;
   const float *ag = a.As + (int64_t)b * a.nC * P;
   if constexpr (SMEM) {
-    stage_table<ND>(s_tab, tg, a.nC);
+    stage_table(s_tab, tg, a.nC * P);
     __syncthreads();
   }
   const float *tab = SMEM ? s_tab : tg;
@@ -135,8 +143,10 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
   const int64_t nP = a.nP;
   const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
   float *pout = a.out + (int64_t)b * ND * nP;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  const int32_t *ord = a.order ? a.order + (a.batched ? (int64_t)b * nP : 0) : nullptr;
+  for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
+       slot += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = point_of(ord, slot);
     float p[ND];
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
@@ -179,12 +189,12 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
   constexpr int S = kSegSteps;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
-  float *s_mom = s_tab + (A_SMEM ? a.nC * Dim<ND>::kStride : 0);
+  float *s_mom = s_tab + (A_SMEM ? a.nC * P : 0);
   const int b = blockIdx.y;
   const int nC = a.nC;
   const float *ag = a.As + (int64_t)b * nC * P;
   float *gm = a.moments + (int64_t)b * nC * P;
-  if constexpr (A_SMEM) stage_table<ND>(s_tab, ag, nC);
+  if constexpr (A_SMEM) stage_table(s_tab, ag, nC * P);
   if constexpr (M_SMEM) {
     for (int i = threadIdx.x; i < nC * P; i += blockDim.x) s_mom[i] = 0.0f;
   }
@@ -202,9 +212,11 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
   const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
   const float *gin = a.grad_out + (int64_t)b * ND * nP;
   float *gp = a.grad_points ? a.grad_points + (int64_t)b * ND * nP : nullptr;
+  const int32_t *ord = a.order ? a.order + (a.batched ? (int64_t)b * nP : 0) : nullptr;
 
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
+       slot += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = point_of(ord, slot);
     float p[ND];
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
@@ -295,6 +307,68 @@ __global__ void k_cell_index(Tess t, const float *__restrict__ pts, int64_t n,
 }
 
 // ---------------------------------------------------------------------------
+// Spatial ordering: a counting sort of the points of every set by initial
+// cell, so that the threads of a warp start in the same or neighbouring cells
+// (shared-memory broadcasts instead of bank conflicts, warp-aggregated moment
+// flushes).  counts is [n_sets, nC] int32 scratch.
+// ---------------------------------------------------------------------------
+
+template <int ND>
+__global__ void k_cell_histogram(Tess t, const float *__restrict__ pts, int64_t nP, int nC,
+                                 int32_t *__restrict__ counts) {
+  const int set = blockIdx.y;
+  const float *p0 = pts + (int64_t)set * ND * nP;
+  int32_t *cnt = counts + (int64_t)set * nC;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(p0 + k * nP + i);
+    atomicAdd(cnt + lookup<ND>(t, p), 1);
+  }
+}
+
+// Exclusive prefix sum of each set's nC counts, in place; one block per set.
+__global__ void __launch_bounds__(1024) k_exclusive_scan(int32_t *__restrict__ counts, int nC) {
+  __shared__ int32_t part[1024];
+  int32_t *cnt = counts + (int64_t)blockIdx.x * nC;
+  const int per = (nC + blockDim.x - 1) / blockDim.x;
+  const int lo = min(nC, (int)threadIdx.x * per), hi = min(nC, lo + per);
+  int32_t sum = 0;
+  for (int c = lo; c < hi; ++c) sum += cnt[c];
+  part[threadIdx.x] = sum;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {  // Hillis-Steele inclusive scan
+    const int32_t v = threadIdx.x >= (unsigned)off ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int32_t run = part[threadIdx.x] - sum;
+  for (int c = lo; c < hi; ++c) {
+    const int32_t v = cnt[c];
+    cnt[c] = run;
+    run += v;
+  }
+}
+
+template <int ND>
+__global__ void k_cell_scatter(Tess t, const float *__restrict__ pts, int64_t nP, int nC,
+                               int32_t *__restrict__ offsets, int32_t *__restrict__ order) {
+  const int set = blockIdx.y;
+  const float *p0 = pts + (int64_t)set * ND * nP;
+  int32_t *off = offsets + (int64_t)set * nC;
+  int32_t *ord = order + (int64_t)set * nP;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(p0 + k * nP + i);
+    ord[atomicAdd(off + lookup<ND>(t, p), 1)] = (int32_t)i;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Launch helpers.
 // ---------------------------------------------------------------------------
 
@@ -349,7 +423,7 @@ cudaError_t launch_wave(K kernel, int threads, size_t smem, const IntegrateArgs 
 
 template <int ND>
 cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
-  const size_t tab = (size_t)a.nC * Dim<ND>::kStride * sizeof(float);
+  const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
   const bool smem = tab <= kFwdSmemBudget;
   if (a.adaptive) {
     return smem ? launch_wave(k_forward<ND, true, true>, kFwdThreads, tab, a, s)
@@ -361,8 +435,8 @@ cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
 
 template <int ND, bool ADAPT>
 cudaError_t backward_nd(const IntegrateArgs &a, cudaStream_t s) {
-  const size_t tab = (size_t)a.nC * Dim<ND>::kStride * sizeof(float);
-  const size_t mom = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  const size_t mom = tab;
   if (tab + mom <= kBwdSmemBudget)
     return launch_wave(k_backward<ND, ADAPT, true, true>, kBwdThreads, tab + mom, a, s);
   if (mom <= kBwdSmemBudget)
@@ -402,6 +476,29 @@ cudaError_t launch_cell_index(int ndim, Tess t, const float *points, int64_t n, 
     case 1: k_cell_index<1><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
     case 2: k_cell_index<2><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
     default: k_cell_index<3><<<(unsigned)blocks, 256, 0, s>>>(t, points, n, cells); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_order_points(int ndim, Tess t, const float *points, int64_t nP, int n_sets,
+                                int nC, int32_t *counts, int32_t *order, cudaStream_t s) {
+  if (nP == 0 || n_sets == 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)n_sets * nC * sizeof(int32_t), s);
+  if (e != cudaSuccess) return e;
+  int64_t bx = (nP + 255) / 256;
+  const int64_t cap = (int64_t)device_info().sm_count * 8;
+  if (bx > cap) bx = cap;
+  const dim3 grid((unsigned)bx, (unsigned)n_sets);
+  switch (ndim) {
+    case 1: k_cell_histogram<1><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
+    case 2: k_cell_histogram<2><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
+    default: k_cell_histogram<3><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
+  }
+  k_exclusive_scan<<<n_sets, 1024, 0, s>>>(counts, nC);
+  switch (ndim) {
+    case 1: k_cell_scatter<1><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
+    case 2: k_cell_scatter<2><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
+    default: k_cell_scatter<3><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
   }
   return cudaGetLastError();
 }

@@ -25,6 +25,7 @@ struct IntegrateArgs {
   float *out;             // forward: [n_theta, ndim, nP]
   float *moments;         // backward: [n_theta, nC, ppc]
   float *grad_points;     // backward: [n_theta, ndim, nP] or nullptr
+  const int32_t *order;   // processing order [1 or n_theta, nP] or nullptr
 };
 
 // Each returns cudaSuccess or the launch error.
@@ -32,6 +33,8 @@ cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_forward_1d(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s);
 
+cudaError_t launch_order_points(int ndim, Tess t, const float *points, int64_t nP, int n_sets,
+                                int nC, int32_t *counts, int32_t *order, cudaStream_t s);
 cudaError_t launch_cell_index(int ndim, Tess t, const float *points, int64_t n, int32_t *cells,
                               cudaStream_t s);
 cudaError_t launch_expm(int ndim, const float *As, int64_t n, float dT, float *trels,

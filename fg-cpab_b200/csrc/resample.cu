@@ -91,14 +91,20 @@ __device__ __forceinline__ float sample3(const float *__restrict__ d, const Loc3
 }
 
 // Backward at one location for one channel: accumulates d(out)/d(weights)
-// times g into gw[] and scatters g * weights into gd (when non-null).
+// times g into gw[] and scatters g * weights into gd (when non-null).  Each
+// product is rounded on its own, as torch's autograd evaluates them, so that
+// g*hi - g*lo is exactly 0 when a coordinate is clamped (hi == lo).
+__device__ __forceinline__ float gdiff(float g, float hi, float lo) {
+  return __fsub_rn(__fmul_rn(g, hi), __fmul_rn(g, lo));
+}
+
 __device__ __forceinline__ void sample_bwd(const float *__restrict__ d, float *__restrict__ gd,
                                            const Loc1 &l, int64_t, float g, float (&gw)[1]) {
   const float c0 = __ldg(d + l.x.lo), c1 = __ldg(d + l.x.hi);
-  gw[0] += g * c1 - g * c0;
+  gw[0] = __fadd_rn(gw[0], gdiff(g, c1, c0));
   if (gd) {
-    atomicAdd(gd + l.x.lo, g * (1.0f - l.x.w));
-    atomicAdd(gd + l.x.hi, g * l.x.w);
+    atomicAdd(gd + l.x.lo, __fmul_rn(g, __fsub_rn(1.0f, l.x.w)));
+    atomicAdd(gd + l.x.hi, __fmul_rn(g, l.x.w));
   }
 }
 
@@ -107,16 +113,16 @@ __device__ __forceinline__ void sample2_bwd(const float *__restrict__ d, float *
   const int64_t a00 = l.x.lo * s1 + l.y.lo, a01 = l.x.lo * s1 + l.y.hi;
   const int64_t a10 = l.x.hi * s1 + l.y.lo, a11 = l.x.hi * s1 + l.y.hi;
   const float c00 = __ldg(d + a00), c01 = __ldg(d + a01), c10 = __ldg(d + a10), c11 = __ldg(d + a11);
-  const float xw = l.x.w, xc = 1.0f - xw, yw = l.y.w, yc = 1.0f - yw;
-  const float g0 = g * yc, g1 = g * yw;  // gradients of the two x-lerps
-  const float c0 = c00 * xc + c10 * xw, c1 = c01 * xc + c11 * xw;
-  gw[0] += (g0 * c10 - g0 * c00) + (g1 * c11 - g1 * c01);
-  gw[1] += g * c1 - g * c0;
+  const float xw = l.x.w, xc = __fsub_rn(1.0f, xw), yw = l.y.w, yc = __fsub_rn(1.0f, yw);
+  const float g0 = __fmul_rn(g, yc), g1 = __fmul_rn(g, yw);  // gradients of the two x-lerps
+  const float c0 = lerp_ref(c00, c10, xw, xc), c1 = lerp_ref(c01, c11, xw, xc);
+  gw[0] = __fadd_rn(gw[0], __fadd_rn(gdiff(g0, c10, c00), gdiff(g1, c11, c01)));
+  gw[1] = __fadd_rn(gw[1], gdiff(g, c1, c0));
   if (gd) {
-    atomicAdd(gd + a00, g0 * xc);
-    atomicAdd(gd + a10, g0 * xw);
-    atomicAdd(gd + a01, g1 * xc);
-    atomicAdd(gd + a11, g1 * xw);
+    atomicAdd(gd + a00, __fmul_rn(g0, xc));
+    atomicAdd(gd + a10, __fmul_rn(g0, xw));
+    atomicAdd(gd + a01, __fmul_rn(g1, xc));
+    atomicAdd(gd + a11, __fmul_rn(g1, xw));
   }
 }
 
@@ -132,23 +138,25 @@ __device__ __forceinline__ void sample3_bwd(const float *__restrict__ d, float *
 #pragma unroll
   for (int k = 0; k < 8; ++k) c[k] = __ldg(d + a[k]);
   // c[k] for k = 4*X + 2*Y + Z.
-  const float xw = l.x.w, xc = 1.0f - xw, yw = l.y.w, yc = 1.0f - yw, zw = l.z.w, zc = 1.0f - zw;
-  const float c00 = c[0] * xc + c[4] * xw;  // (y0, z0)
-  const float c01 = c[1] * xc + c[5] * xw;  // (y0, z1)
-  const float c10 = c[2] * xc + c[6] * xw;  // (y1, z0)
-  const float c11 = c[3] * xc + c[7] * xw;  // (y1, z1)
-  const float c0 = c00 * yc + c10 * yw, c1 = c01 * yc + c11 * yw;
-  const float gc0 = g * zc, gc1 = g * zw;
-  const float g00 = gc0 * yc, g10 = gc0 * yw, g01 = gc1 * yc, g11 = gc1 * yw;
-  gw[2] += g * c1 - g * c0;
-  gw[1] += (gc0 * c10 - gc0 * c00) + (gc1 * c11 - gc1 * c01);
-  gw[0] += (g00 * c[4] - g00 * c[0]) + (g01 * c[5] - g01 * c[1]) + (g10 * c[6] - g10 * c[2]) +
-           (g11 * c[7] - g11 * c[3]);
+  const float xw = l.x.w, xc = __fsub_rn(1.0f, xw), yw = l.y.w, yc = __fsub_rn(1.0f, yw);
+  const float zw = l.z.w, zc = __fsub_rn(1.0f, zw);
+  const float c00 = lerp_ref(c[0], c[4], xw, xc);  // (y0, z0)
+  const float c01 = lerp_ref(c[1], c[5], xw, xc);  // (y0, z1)
+  const float c10 = lerp_ref(c[2], c[6], xw, xc);  // (y1, z0)
+  const float c11 = lerp_ref(c[3], c[7], xw, xc);  // (y1, z1)
+  const float c0 = lerp_ref(c00, c10, yw, yc), c1 = lerp_ref(c01, c11, yw, yc);
+  const float gc0 = __fmul_rn(g, zc), gc1 = __fmul_rn(g, zw);
+  const float g00 = __fmul_rn(gc0, yc), g10 = __fmul_rn(gc0, yw);
+  const float g01 = __fmul_rn(gc1, yc), g11 = __fmul_rn(gc1, yw);
+  gw[2] = __fadd_rn(gw[2], gdiff(g, c1, c0));
+  gw[1] = __fadd_rn(gw[1], __fadd_rn(gdiff(gc0, c10, c00), gdiff(gc1, c11, c01)));
+  gw[0] = __fadd_rn(gw[0], __fadd_rn(__fadd_rn(gdiff(g00, c[4], c[0]), gdiff(g01, c[5], c[1])),
+                                     __fadd_rn(gdiff(g10, c[6], c[2]), gdiff(g11, c[7], c[3]))));
   if (gd) {
-    atomicAdd(gd + a[0], g00 * xc); atomicAdd(gd + a[4], g00 * xw);
-    atomicAdd(gd + a[1], g01 * xc); atomicAdd(gd + a[5], g01 * xw);
-    atomicAdd(gd + a[2], g10 * xc); atomicAdd(gd + a[6], g10 * xw);
-    atomicAdd(gd + a[3], g11 * xc); atomicAdd(gd + a[7], g11 * xw);
+    atomicAdd(gd + a[0], __fmul_rn(g00, xc)); atomicAdd(gd + a[4], __fmul_rn(g00, xw));
+    atomicAdd(gd + a[1], __fmul_rn(g01, xc)); atomicAdd(gd + a[5], __fmul_rn(g01, xw));
+    atomicAdd(gd + a[2], __fmul_rn(g10, xc)); atomicAdd(gd + a[6], __fmul_rn(g10, xw));
+    atomicAdd(gd + a[3], __fmul_rn(g11, xc)); atomicAdd(gd + a[7], __fmul_rn(g11, xw));
   }
 }
 
@@ -186,7 +194,7 @@ __global__ void k_interp1d_bwd(ResampleArgs a) {
       const float g = __ldg(a.grad_out + ((int64_t)b * C + ch) * n0 + i);
       sample_bwd(a.data + base, a.grad_data ? a.grad_data + base : nullptr, l, 0, g, gw);
     }
-    if (a.grad_grid) a.grad_grid[(int64_t)b * n0 + i] = gw[0] * top;
+    if (a.grad_grid) a.grad_grid[(int64_t)b * n0 + i] = __fmul_rn(gw[0], top);
   }
 }
 
@@ -234,8 +242,8 @@ __global__ void __launch_bounds__(kTile *kRows) k_interp2d(ResampleArgs a) {
           sample2_bwd(a.data + bc * S0 * S1, a.grad_data ? a.grad_data + bc * S0 * S1 : nullptr,
                       l, S1, g, gw);
         }
-        sd[0][tx][r] = gw[0] * (float)(S0 - 1);
-        sd[1][tx][r] = gw[1] * (float)(S1 - 1);
+        sd[0][tx][r] = __fmul_rn(gw[0], (float)(S0 - 1));
+        sd[1][tx][r] = __fmul_rn(gw[1], (float)(S1 - 1));
       }
     }
   }
@@ -303,9 +311,9 @@ __global__ void __launch_bounds__(kTile *kRows) k_interp3d(ResampleArgs a) {
                       S2, g, gw);
         }
         // Reuse the grid tile for d grid (each entry is read only by its owner).
-        sg[0][tx][r] = gw[0] * (float)(S0 - 1);
-        sg[1][tx][r] = gw[1] * (float)(S1 - 1);
-        sg[2][tx][r] = gw[2] * (float)(S2 - 1);
+        sg[0][tx][r] = __fmul_rn(gw[0], (float)(S0 - 1));
+        sg[1][tx][r] = __fmul_rn(gw[1], (float)(S1 - 1));
+        sg[2][tx][r] = __fmul_rn(gw[2], (float)(S2 - 1));
       }
     }
   }

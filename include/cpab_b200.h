@@ -89,13 +89,17 @@ int cpab_b200_build_A(int ndim, int64_t nC, int64_t d, int n_theta,
  * p <- trels[cell(p)] [p; 1]; with adaptive = 1 a step that changes cell is
  * replaced by one Heun step on the velocity fields As.  `points_batched` = 1
  * when points is [n_theta, ndim, nP], 0 when it is [ndim, nP].  out is
- * [n_theta, ndim, nP].  nc has ndim entries.  For ndim == 1 this forwards to
+ * [n_theta, ndim, nP].  nc has ndim entries.  `order` (may be NULL) is a
+ * processing order from cpab_b200_order_points: [1, nP] for shared points,
+ * [n_theta, nP] for batched ones; it changes only which thread handles which
+ * point, never a result.  For ndim == 1 this forwards to
  * cpab_b200_forward_1d_closed_form (trels and nstepsolver are then unused),
  * like the reference's dispatch.
  * Replaces cpab/pytorch/transformer_cuda.cpp:32-61 (cpab_forward).
  */
 int cpab_b200_forward(int ndim, const int32_t *nc, const float *points,
-                      int64_t nP, int points_batched, const float *trels,
+                      int64_t nP, int points_batched, const int32_t *order,
+                      const float *trels,
                       const float *As, int n_theta, int nstepsolver,
                       int adaptive, float *out, cpab_stream_t stream);
 
@@ -104,7 +108,8 @@ int cpab_b200_forward(int ndim, const int32_t *nc, const float *points,
  * Replaces cpab/pytorch/transformer_cuda.cpp:66-85.
  */
 int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP,
-                                     int points_batched, const float *As,
+                                     int points_batched, const int32_t *order,
+                                     const float *As,
                                      int n_theta, int ncx, float *out,
                                      cpab_stream_t stream);
 
@@ -119,10 +124,24 @@ int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP,
  * Replaces cpab/pytorch/transformer_cuda.cpp:92-116 and :122-153.
  */
 int cpab_b200_backward(int ndim, const int32_t *nc, const float *points,
-                       int64_t nP, int points_batched, const float *As,
+                       int64_t nP, int points_batched, const int32_t *order,
+                       const float *As,
                        int n_theta, const float *grad_out, int nstepsolver,
                        int adaptive, float *moments, float *grad_points,
                        cpab_stream_t stream);
+
+/*
+ * order[s, :] = the points of set s (s < n_sets; points [n_sets, ndim, nP],
+ * or [ndim, nP] with n_sets = 1) sorted by the cell that contains them
+ * (counting sort; ties in arbitrary order).  Passing it to forward/backward
+ * makes the threads of a warp start in the same or adjacent cells.
+ * counts_scratch is caller-provided scratch of n_sets * nC int32; order is
+ * [n_sets, nP] int32.  No counterpart in the reference (its kernels take the
+ * points in storage order).
+ */
+int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points,
+                           int64_t nP, int n_sets, int32_t *counts_scratch,
+                           int32_t *order, cpab_stream_t stream);
 
 /*
  * cells[i] = index of the tessellation cell containing points[:, i]

@@ -150,17 +150,29 @@ void oracle_cells(int nd, const int32_t *nc, const float *pts, int64_t n, int32_
 }
 
 /* ------------------------------------------------------------------ expm */
+/* Sums of products are evaluated left to right, the first two products fused
+ * as fmaf(a, b, c*d) and every further product fused onto the running sum:
+ * the rounding of the reference's compiled expm kernels (verified bit for bit
+ * against Trels they produced on a B200, tests/golden/kernel_golden.npz). */
+
+static float dot2(float a, float b, float c, float d) { return fmaf(a, b, c * d); }
+static float dot3(float a, float b, float c, float d, float e, float f) {
+  return fmaf(e, f, fmaf(a, b, c * d));
+}
+static float diff2(float a, float b, float c, float d) { return fmaf(a, b, -(c * d)); }
+static float pdiag(float h, float m, float s, float q) { return fmaf(s, q, fmaf(h, m, 1.0f)); }
+static float poff(float h, float m, float s, float q) { return fmaf(h, m, s * q); }
 
 static void expm1d(const float *A, float dT, float *out) {
   float m00 = dT * A[0], m01 = dT * A[1];
-  float e = expf(m00), rel;
+  float rel;
   if (fabsf(m00) > 1e-6f) {
     rel = expm1f(m00) / m00;
   } else {
     float q = m00 * m00;
-    rel = 1.0f + 0.5f * m00 + (1.0f / 6.0f) * q + (1.0f / 24.0f) * q * m00;
+    rel = fmaf((1.0f / 24.0f) * q, m00, fmaf(1.0f / 6.0f, q, fmaf(0.5f, m00, 1.0f)));
   }
-  out[0] = e;
+  out[0] = expf(m00);
   out[1] = m01 * rel;
 }
 
@@ -169,27 +181,28 @@ static int n_squarings(float norm) { return norm > 0.5f ? (int)ceilf(log2f(norm 
 static void expm2d(const float *A, float dT, float *out) {
   float a[6];
   for (int k = 0; k < 6; ++k) a[k] = dT * A[k];
-  float nrm = sqrtf(a[0] * a[0] + a[1] * a[1] + a[2] * a[2] + a[3] * a[3] + a[4] * a[4] + a[5] * a[5]);
-  int ns = n_squarings(nrm);
+  float sq = dot2(a[0], a[0], a[1], a[1]);
+  for (int k = 2; k < 6; ++k) sq = fmaf(a[k], a[k], sq);
+  int ns = n_squarings(sqrtf(sq));
   float sc = 1.0f;
   for (int i = 0; i < ns; ++i) sc *= 0.5f;
   float m00 = a[0] * sc, m01 = a[1] * sc, m02 = a[2] * sc;
   float m10 = a[3] * sc, m11 = a[4] * sc, m12 = a[5] * sc;
-  float q00 = m00 * m00 + m01 * m10, q01 = m00 * m01 + m01 * m11, q02 = m00 * m02 + m01 * m12;
-  float q10 = m10 * m00 + m11 * m10, q11 = m10 * m01 + m11 * m11, q12 = m10 * m02 + m11 * m12;
+  float q00 = dot2(m00, m00, m01, m10), q01 = dot2(m00, m01, m01, m11), q02 = dot2(m00, m02, m01, m12);
+  float q10 = dot2(m10, m00, m11, m10), q11 = dot2(m10, m01, m11, m11), q12 = dot2(m10, m02, m11, m12);
   const float t = 1.0f / 12.0f;
-  float P00 = 1.0f + 0.5f * m00 + t * q00, P01 = 0.5f * m01 + t * q01, P02 = 0.5f * m02 + t * q02;
-  float P10 = 0.5f * m10 + t * q10, P11 = 1.0f + 0.5f * m11 + t * q11, P12 = 0.5f * m12 + t * q12;
-  float Q00 = 1.0f - 0.5f * m00 + t * q00, Q01 = -0.5f * m01 + t * q01, Q02 = -0.5f * m02 + t * q02;
-  float Q10 = -0.5f * m10 + t * q10, Q11 = 1.0f - 0.5f * m11 + t * q11, Q12 = -0.5f * m12 + t * q12;
-  float inv = 1.0f / (Q00 * Q11 - Q01 * Q10);
+  float P00 = pdiag(0.5f, m00, t, q00), P01 = poff(0.5f, m01, t, q01), P02 = poff(0.5f, m02, t, q02);
+  float P10 = poff(0.5f, m10, t, q10), P11 = pdiag(0.5f, m11, t, q11), P12 = poff(0.5f, m12, t, q12);
+  float Q00 = pdiag(-0.5f, m00, t, q00), Q01 = poff(-0.5f, m01, t, q01), Q02 = poff(-0.5f, m02, t, q02);
+  float Q10 = poff(-0.5f, m10, t, q10), Q11 = pdiag(-0.5f, m11, t, q11), Q12 = poff(-0.5f, m12, t, q12);
+  float inv = 1.0f / diff2(Q00, Q11, Q01, Q10);
   float i00 = Q11 * inv, i01 = -Q01 * inv, i10 = -Q10 * inv, i11 = Q00 * inv;
-  float i02 = -(i00 * Q02 + i01 * Q12), i12 = -(i10 * Q02 + i11 * Q12);
-  float r00 = i00 * P00 + i01 * P10, r01 = i00 * P01 + i01 * P11, r02 = i00 * P02 + i01 * P12 + i02;
-  float r10 = i10 * P00 + i11 * P10, r11 = i10 * P01 + i11 * P11, r12 = i10 * P02 + i11 * P12 + i12;
+  float i02 = -dot2(i00, Q02, i01, Q12), i12 = -dot2(i10, Q02, i11, Q12);
+  float r00 = dot2(i00, P00, i01, P10), r01 = dot2(i00, P01, i01, P11), r02 = dot2(i00, P02, i01, P12) + i02;
+  float r10 = dot2(i10, P00, i11, P10), r11 = dot2(i10, P01, i11, P11), r12 = dot2(i10, P02, i11, P12) + i12;
   for (int s = 0; s < ns; ++s) {
-    float n00 = r00 * r00 + r01 * r10, n01 = r00 * r01 + r01 * r11, n02 = r00 * r02 + r01 * r12 + r02;
-    float n10 = r10 * r00 + r11 * r10, n11 = r10 * r01 + r11 * r11, n12 = r10 * r02 + r11 * r12 + r12;
+    float n00 = dot2(r00, r00, r01, r10), n01 = dot2(r00, r01, r01, r11), n02 = dot2(r00, r02, r01, r12) + r02;
+    float n10 = dot2(r10, r00, r11, r10), n11 = dot2(r10, r01, r11, r11), n12 = dot2(r10, r02, r11, r12) + r12;
     r00 = n00; r01 = n01; r02 = n02; r10 = n10; r11 = n11; r12 = n12;
   }
   out[0] = r00; out[1] = r01; out[2] = r02; out[3] = r10; out[4] = r11; out[5] = r12;
@@ -197,12 +210,10 @@ static void expm2d(const float *A, float dT, float *out) {
 
 static void expm3d(const float *A, float dT, float *out) {
   float m[3][4];
-  float sq = 0.0f;
   for (int i = 0; i < 3; ++i)
-    for (int j = 0; j < 4; ++j) {
-      m[i][j] = dT * A[i * 4 + j];
-      sq += m[i][j] * m[i][j];
-    }
+    for (int j = 0; j < 4; ++j) m[i][j] = dT * A[i * 4 + j];
+  float sq = dot2(m[0][0], m[0][0], m[0][1], m[0][1]);
+  for (int k = 2; k < 12; ++k) sq = fmaf(m[k / 4][k % 4], m[k / 4][k % 4], sq);
   int ns = n_squarings(sqrtf(sq));
   float sc = 1.0f;
   for (int i = 0; i < ns; ++i) sc *= 0.5f;
@@ -210,50 +221,44 @@ static void expm3d(const float *A, float dT, float *out) {
     for (int j = 0; j < 4; ++j) m[i][j] *= sc;
   float q[3][3], qt[3];
   for (int i = 0; i < 3; ++i) {
-    for (int j = 0; j < 3; ++j) q[i][j] = m[i][0] * m[0][j] + m[i][1] * m[1][j] + m[i][2] * m[2][j];
-    qt[i] = m[i][0] * m[0][3] + m[i][1] * m[1][3] + m[i][2] * m[2][3];
+    for (int j = 0; j < 3; ++j) q[i][j] = dot3(m[i][0], m[0][j], m[i][1], m[1][j], m[i][2], m[2][j]);
+    qt[i] = dot3(m[i][0], m[0][3], m[i][1], m[1][3], m[i][2], m[2][3]);
   }
   const float t12 = 1.0f / 12.0f;
   float P[3][3], Q[3][3], pt[3], qtt[3];
   for (int i = 0; i < 3; ++i) {
     for (int j = 0; j < 3; ++j) {
-      if (i == j) {
-        P[i][j] = 1.0f + 0.5f * m[i][j] + t12 * q[i][j];
-        Q[i][j] = 1.0f - 0.5f * m[i][j] + t12 * q[i][j];
-      } else {
-        P[i][j] = 0.5f * m[i][j] + t12 * q[i][j];
-        Q[i][j] = -0.5f * m[i][j] + t12 * q[i][j];
-      }
+      P[i][j] = i == j ? pdiag(0.5f, m[i][j], t12, q[i][j]) : poff(0.5f, m[i][j], t12, q[i][j]);
+      Q[i][j] = i == j ? pdiag(-0.5f, m[i][j], t12, q[i][j]) : poff(-0.5f, m[i][j], t12, q[i][j]);
     }
-    pt[i] = 0.5f * m[i][3] + t12 * qt[i];
-    qtt[i] = -0.5f * m[i][3] + t12 * qt[i];
+    pt[i] = poff(0.5f, m[i][3], t12, qt[i]);
+    qtt[i] = poff(-0.5f, m[i][3], t12, qt[i]);
   }
-  float det = Q[0][0] * (Q[1][1] * Q[2][2] - Q[1][2] * Q[2][1]) -
-              Q[0][1] * (Q[1][0] * Q[2][2] - Q[1][2] * Q[2][0]) +
-              Q[0][2] * (Q[1][0] * Q[2][1] - Q[1][1] * Q[2][0]);
-  float id = 1.0f / det;
+  float c0 = diff2(Q[1][1], Q[2][2], Q[1][2], Q[2][1]);
+  float c1 = diff2(Q[1][0], Q[2][2], Q[1][2], Q[2][0]);
+  float c2 = diff2(Q[1][0], Q[2][1], Q[1][1], Q[2][0]);
+  float id = 1.0f / fmaf(Q[0][2], c2, fmaf(Q[0][0], c0, -(Q[0][1] * c1)));
   float I[3][3];
-  I[0][0] = (Q[1][1] * Q[2][2] - Q[1][2] * Q[2][1]) * id;
-  I[0][1] = (Q[0][2] * Q[2][1] - Q[0][1] * Q[2][2]) * id;
-  I[0][2] = (Q[0][1] * Q[1][2] - Q[0][2] * Q[1][1]) * id;
-  I[1][0] = (Q[1][2] * Q[2][0] - Q[1][0] * Q[2][2]) * id;
-  I[1][1] = (Q[0][0] * Q[2][2] - Q[0][2] * Q[2][0]) * id;
-  I[1][2] = (Q[0][2] * Q[1][0] - Q[0][0] * Q[1][2]) * id;
-  I[2][0] = (Q[1][0] * Q[2][1] - Q[1][1] * Q[2][0]) * id;
-  I[2][1] = (Q[0][1] * Q[2][0] - Q[0][0] * Q[2][1]) * id;
-  I[2][2] = (Q[0][0] * Q[1][1] - Q[0][1] * Q[1][0]) * id;
-  float it[3];
-  for (int i = 0; i < 3; ++i) it[i] = -(I[i][0] * qtt[0] + I[i][1] * qtt[1] + I[i][2] * qtt[2]);
+  I[0][0] = c0 * id;
+  I[0][1] = diff2(Q[0][2], Q[2][1], Q[0][1], Q[2][2]) * id;
+  I[0][2] = diff2(Q[0][1], Q[1][2], Q[0][2], Q[1][1]) * id;
+  I[1][0] = diff2(Q[1][2], Q[2][0], Q[1][0], Q[2][2]) * id;
+  I[1][1] = diff2(Q[0][0], Q[2][2], Q[0][2], Q[2][0]) * id;
+  I[1][2] = diff2(Q[0][2], Q[1][0], Q[0][0], Q[1][2]) * id;
+  I[2][0] = c2 * id;
+  I[2][1] = diff2(Q[0][1], Q[2][0], Q[0][0], Q[2][1]) * id;
+  I[2][2] = diff2(Q[0][0], Q[1][1], Q[0][1], Q[1][0]) * id;
   float R[3][3], rt[3];
   for (int i = 0; i < 3; ++i) {
-    for (int j = 0; j < 3; ++j) R[i][j] = I[i][0] * P[0][j] + I[i][1] * P[1][j] + I[i][2] * P[2][j];
-    rt[i] = I[i][0] * pt[0] + I[i][1] * pt[1] + I[i][2] * pt[2] + it[i];
+    float it = -dot3(I[i][0], qtt[0], I[i][1], qtt[1], I[i][2], qtt[2]);
+    for (int j = 0; j < 3; ++j) R[i][j] = dot3(I[i][0], P[0][j], I[i][1], P[1][j], I[i][2], P[2][j]);
+    rt[i] = dot3(I[i][0], pt[0], I[i][1], pt[1], I[i][2], pt[2]) + it;
   }
   for (int s = 0; s < ns; ++s) {
     float N[3][3], nt[3];
     for (int i = 0; i < 3; ++i) {
-      for (int j = 0; j < 3; ++j) N[i][j] = R[i][0] * R[0][j] + R[i][1] * R[1][j] + R[i][2] * R[2][j];
-      nt[i] = R[i][0] * rt[0] + R[i][1] * rt[1] + R[i][2] * rt[2] + rt[i];
+      for (int j = 0; j < 3; ++j) N[i][j] = dot3(R[i][0], R[0][j], R[i][1], R[1][j], R[i][2], R[2][j]);
+      nt[i] = dot3(R[i][0], rt[0], R[i][1], rt[1], R[i][2], rt[2]) + rt[i];
     }
     memcpy(R, N, sizeof(R));
     memcpy(rt, nt, sizeof(rt));
@@ -522,6 +527,24 @@ void oracle_midpoint_forward(int nd, const int32_t *nc, const float *pts, int64_
       for (int k = 0; k < nd; ++k) p[k] = src[k * nP + i];
       for (int n = 0; n < T; ++n) replay(nd, ts, As + (int64_t)b * nC * P, p, h, hh, adaptive);
       for (int k = 0; k < nd; ++k) out[(int64_t)b * nd * nP + k * nP + i] = p[k];
+    }
+  }
+}
+
+/* out[t, r] = sum over row r of a CSR matrix of vals * x[t, col], accumulated
+ * in float32 with fmaf in stored (column) order: an fp32 sparse product as the
+ * reference's torch.sparse.mm computes A = B theta^T and dtheta = B^T m
+ * (cpab/pytorch/transformer.py:84, :166). */
+void oracle_csr_matmul(int64_t rows, const int32_t *rowptr, const int32_t *colidx,
+                       const float *vals, int n_rhs, const float *x, int64_t x_stride,
+                       float *out, int64_t out_stride) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int t = 0; t < n_rhs; ++t) {
+    for (int64_t r = 0; r < rows; ++r) {
+      const float *xt = x + (int64_t)t * x_stride;
+      float s = 0.0f;
+      for (int32_t k = rowptr[r]; k < rowptr[r + 1]; ++k) s = fmaf(vals[k], xt[colidx[k]], s);
+      out[(int64_t)t * out_stride + r] = s;
     }
   }
 }

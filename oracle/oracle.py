@@ -5,9 +5,9 @@ CPU-baseline legs of bench.py, as the checker -- never by the product.
 
   * integration / adjoint / expm / cell lookup: liboracle.so, the C
     restatement in cpab_oracle.c (cpab/core/cpab_ops_{1,2,3}d.cu);
-  * A = B theta and dtheta = B^T m: scipy sparse products in float64, rounded
-    to float32 (cpab/pytorch/transformer.py:84-88, :165-166 use
-    torch.sparse.mm);
+  * A = B theta and dtheta = B^T m: fp32 CSR products (fma in stored order),
+    as torch.sparse.mm computes them in cpab/pytorch/transformer.py:84-88,
+    :165-166;
   * resampling: numpy float32 restatement of cpab/pytorch/interpolation.py:8-160
     (forward, op for op) and of the gradient its autograd graph produces.
 
@@ -46,6 +46,8 @@ def lib():
         L.oracle_midpoint_forward.argtypes = [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _c_int,
                                               _c_int, _p]
         L.oracle_midpoint_forward.restype = None
+        L.oracle_csr_matmul.argtypes = [_c_i64, _p, _p, _p, _c_int, _p, _c_i64, _p, _c_i64]
+        L.oracle_csr_matmul.restype = None
         L.oracle_num_threads.restype = _c_int
         L.oracle_set_num_threads.argtypes = [_c_int]
         for fn in (L.oracle_cells, L.oracle_expm, L.oracle_forward, L.oracle_backward):
@@ -98,18 +100,35 @@ def expm(As, dT):
     return out
 
 
+def _csr32(M):
+    M = M.tocsr().astype(np.float32)
+    M.sort_indices()
+    return (np.ascontiguousarray(M.indptr, np.int32), np.ascontiguousarray(M.indices, np.int32),
+            np.ascontiguousarray(M.data, np.float32))
+
+
+def csr_matmul(M, X):
+    """(M @ X^T)^T for a sparse M [rows, cols] and X [n, cols], fp32 fma in CSR order."""
+    X = _f32(X)
+    rp, ci, v = _csr32(M)
+    rows = M.shape[0]
+    out = np.empty((X.shape[0], rows), dtype=np.float32)
+    lib().oracle_csr_matmul(rows, _ptr(rp), _ptr(ci), _ptr(v), X.shape[0], _ptr(X), X.shape[1],
+                            _ptr(out), rows)
+    return out
+
+
 def build_A(basis, theta, ndim):
-    """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T."""
-    th = np.asarray(theta, dtype=np.float64)
-    A = (basis.astype(np.float64) @ th.T).T
+    """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T (fp32)."""
+    th = _f32(theta)
     nC = basis.shape[0] // (ndim * (ndim + 1))
-    return _f32(A.reshape(th.shape[0], nC, ndim, ndim + 1))
+    return csr_matmul(basis, th).reshape(th.shape[0], nC, ndim, ndim + 1)
 
 
 def project(basis, moments):
-    """dtheta [n_theta, d] = B^T vec(moments)."""
-    m = np.asarray(moments, dtype=np.float64).reshape(moments.shape[0], -1)
-    return _f32((basis.T.astype(np.float64) @ m.T).T)
+    """dtheta [n_theta, d] = B^T vec(moments) (fp32)."""
+    m = _f32(moments).reshape(moments.shape[0], -1)
+    return csr_matmul(basis.T, m)
 
 
 def integrate(nc, points, As, trels, nstepsolver=50, adaptive=False):
@@ -226,41 +245,78 @@ def interpolate(ndim, data, grid, outsize):
     return np.ascontiguousarray(c.reshape(B, n2, n1, n0, C).transpose(0, 4, 3, 2, 1))
 
 
+def _gdiff(g, hi, lo):
+    """sum_ch(g*hi) - sum_ch(g*lo), float32 (autograd's two product edges)."""
+    f = np.float32
+    return (g * hi).astype(f).sum(-1, dtype=f) - (g * lo).astype(f).sum(-1, dtype=f)
+
+
 def interpolate_backward(ndim, data, grid, outsize, grad_out):
-    """Gradients (d grid [B, ndim, P], d data [B, C, *in]) of interpolate,
-    accumulated in float64."""
-    data = np.asarray(data, dtype=np.float64)
+    """Gradients (d grid [B, ndim, P], d data [B, C, *in]) of interpolate.
+
+    d grid restates, in float32, the autograd graph of the reference's
+    expressions (c = c0*(1-w) + c1*w nested per axis): per axis the gradient
+    of the weight is sum_ch(g*hi) - sum_ch(g*lo) with g the incoming gradient
+    of that lerp, then times (in_size-1).  d data is the scatter-add of
+    g * weights, accumulated in float64."""
+    f = np.float32
+    data = _f32(data)
     grid = _f32(grid)
     B, C = data.shape[:2]
     P = grid.shape[2]
-    g = np.asarray(grad_out, dtype=np.float64)
+    g = _f32(grad_out)
     # [B, C, *outsize] -> [B, P, C] with P in grid order (coordinate 0 fastest)
     g = g.reshape(B, C, -1).transpose(0, 2, 1) if ndim == 1 else np.moveaxis(g, 1, -1).transpose(
         *([0] + list(range(ndim, 0, -1)) + [ndim + 1])).reshape(B, P, C)
-    dgrid = np.zeros((B, ndim, P))
-    ddata = np.zeros_like(data)
+    g = np.ascontiguousarray(g, dtype=f)
     bidx = np.arange(B)[:, None]
     axes = [_axis(grid[:, k], data.shape[2 + k]) for k in range(ndim)]
-    # corner weights per axis: (index, weight, derivative sign)
-    import itertools
-    for corner in itertools.product((0, 1), repeat=ndim):
-        idx, w, dw = [], np.ones((B, P)), []
-        for k, bit in enumerate(corner):
-            lo, hi, wk = axes[k]
-            wk = wk.astype(np.float64)
-            idx.append(hi if bit else lo)
-            w = w * (wk if bit else 1.0 - wk)
-        vals = data[(bidx, slice(None)) + tuple(idx)]          # [B, P, C]
-        gv = (g * vals).sum(-1)                                 # [B, P]
-        for k, bit in enumerate(corner):
-            wk = axes[k][2].astype(np.float64)
-            others = np.ones((B, P))
-            for j, bj in enumerate(corner):
-                if j != k:
-                    wj = axes[j][2].astype(np.float64)
-                    others = others * (wj if bj else 1.0 - wj)
-            dgrid[:, k] += (1.0 if bit else -1.0) * others * gv * (data.shape[2 + k] - 1)
-        contrib = g * w[..., None]                              # [B, P, C]
+    one = f(1.0)
+    dgrid = np.zeros((B, ndim, P), dtype=f)
+    ddata = np.zeros(data.shape, dtype=np.float64)
+
+    def corner(*bits):
+        return data[(bidx, slice(None)) + tuple(axes[k][1] if b else axes[k][0]
+                                                for k, b in enumerate(bits))]
+
+    def scatter(bits, val):
+        idx = tuple(axes[k][1] if b else axes[k][0] for k, b in enumerate(bits))
         for b in range(B):
-            np.add.at(ddata[b], (slice(None),) + tuple(i[b] for i in idx), contrib[b].T)
-    return dgrid.astype(np.float32), ddata.astype(np.float32)
+            np.add.at(ddata[b], (slice(None),) + tuple(i[b] for i in idx), val[b].T)
+
+    w = [a[2][..., None] for a in axes]
+    wc = [(one - a[2])[..., None] for a in axes]
+    if ndim == 1:
+        c0, c1 = corner(0), corner(1)
+        dgrid[:, 0] = _gdiff(g, c1, c0)
+        scatter((0,), g * wc[0])
+        scatter((1,), g * w[0])
+    elif ndim == 2:
+        c00, c01, c10, c11 = corner(0, 0), corner(0, 1), corner(1, 0), corner(1, 1)
+        c0 = _lerp(c00, c10, w[0])
+        c1 = _lerp(c01, c11, w[0])
+        g0, g1 = (g * wc[1]).astype(f), (g * w[1]).astype(f)
+        dgrid[:, 0] = _gdiff(g0, c10, c00) + _gdiff(g1, c11, c01)
+        dgrid[:, 1] = _gdiff(g, c1, c0)
+        for bits, val in (((0, 0), g0 * wc[0]), ((1, 0), g0 * w[0]), ((0, 1), g1 * wc[0]),
+                          ((1, 1), g1 * w[0])):
+            scatter(bits, val)
+    else:
+        c = {bits: corner(*bits) for bits in __import__("itertools").product((0, 1), repeat=3)}
+        # lerp along x at each (y, z)
+        cx = {(y, z): _lerp(c[(0, y, z)], c[(1, y, z)], w[0]) for y in (0, 1) for z in (0, 1)}
+        c0 = _lerp(cx[(0, 0)], cx[(1, 0)], w[1])
+        c1 = _lerp(cx[(0, 1)], cx[(1, 1)], w[1])
+        gc0, gc1 = (g * wc[2]).astype(f), (g * w[2]).astype(f)
+        dgrid[:, 2] = _gdiff(g, c1, c0)
+        dgrid[:, 1] = _gdiff(gc0, cx[(1, 0)], cx[(0, 0)]) + _gdiff(gc1, cx[(1, 1)], cx[(0, 1)])
+        gy = {(0, 0): (gc0 * wc[1]).astype(f), (1, 0): (gc0 * w[1]).astype(f),
+              (0, 1): (gc1 * wc[1]).astype(f), (1, 1): (gc1 * w[1]).astype(f)}
+        dgrid[:, 0] = sum(_gdiff(gy[(y, z)], c[(1, y, z)], c[(0, y, z)])
+                          for z in (0, 1) for y in (0, 1))
+        for (y, z), gv in gy.items():
+            scatter((0, y, z), gv * wc[0])
+            scatter((1, y, z), gv * w[0])
+    for k in range(ndim):
+        dgrid[:, k] = dgrid[:, k] * f(data.shape[2 + k] - 1)
+    return dgrid, ddata.astype(f)

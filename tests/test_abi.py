@@ -41,15 +41,15 @@ P = ctypes.c_void_p(16)  # never dereferenced: validation fails first
 
 
 @pytest.mark.parametrize("args,code,msg", [
-    ((4, NC2, P, 10, 0, P, P, 1, 50, 0, P, None), -1, "ndim"),
-    ((2, NC2, P, 10, 0, P, P, 1, 0, 0, P, None), -2, "nstepsolver"),
-    ((2, NC2, P, 10, 0, P, P, 1, 257, 0, P, None), -2, "nstepsolver"),
-    ((2, NC2, P, 10, 0, P, P, 1, 50, 2, P, None), -1, "adaptive"),
-    ((2, NC2, P, 10, 2, P, P, 1, 50, 0, P, None), -1, "points_batched"),
-    ((2, NC2, P, 10, 0, P, P, 70000, 50, 0, P, None), -4, "n_theta"),
-    ((2, NC2, P, -1, 0, P, P, 1, 50, 0, P, None), -1, "negative"),
-    ((2, NC2, None, 10, 0, P, P, 1, 50, 0, P, None), -1, "null"),
-    ((2, NC2, P, 10, 0, None, P, 1, 50, 0, P, None), -1, "trels"),
+    ((4, NC2, P, 10, 0, None, P, P, 1, 50, 0, P, None), -1, "ndim"),
+    ((2, NC2, P, 10, 0, None, P, P, 1, 0, 0, P, None), -2, "nstepsolver"),
+    ((2, NC2, P, 10, 0, None, P, P, 1, 257, 0, P, None), -2, "nstepsolver"),
+    ((2, NC2, P, 10, 0, None, P, P, 1, 50, 2, P, None), -1, "adaptive"),
+    ((2, NC2, P, 10, 2, None, P, P, 1, 50, 0, P, None), -1, "points_batched"),
+    ((2, NC2, P, 10, 0, None, P, P, 70000, 50, 0, P, None), -4, "n_theta"),
+    ((2, NC2, P, -1, 0, None, P, P, 1, 50, 0, P, None), -1, "negative"),
+    ((2, NC2, None, 10, 0, None, P, P, 1, 50, 0, P, None), -1, "null"),
+    ((2, NC2, P, 10, 0, None, None, P, 1, 50, 0, P, None), -1, "trels"),
 ])
 def test_forward_argument_errors(args, code, msg):
     L = _native.lib()
@@ -59,16 +59,18 @@ def test_forward_argument_errors(args, code, msg):
 
 def test_zero_sized_calls_succeed_without_work():
     L = _native.lib()
-    assert L.cpab_b200_forward(2, NC2, P, 0, 0, P, P, 3, 50, 0, P, None) == 0
-    assert L.cpab_b200_forward(2, NC2, P, 10, 0, P, P, 0, 50, 0, P, None) == 0
+    assert L.cpab_b200_forward(2, NC2, P, 0, 0, None, P, P, 3, 50, 0, P, None) == 0
+    assert L.cpab_b200_forward(2, NC2, P, 10, 0, None, P, P, 0, 50, 0, P, None) == 0
     assert L.cpab_b200_last_error().decode() == ""
 
 
 def test_other_entry_points_validate():
     L = _native.lib()
     bad = (ctypes.c_int32 * 2)(0, 4)
-    assert L.cpab_b200_backward(2, bad, P, 10, 0, P, 1, P, 50, 0, P, None, None) == -1
-    assert L.cpab_b200_backward(2, NC2, P, 10, 0, P, 1, P, 50, 0, None, None, None) == -1
+    assert L.cpab_b200_backward(2, bad, P, 10, 0, None, P, 1, P, 50, 0, P, None, None) == -1
+    assert L.cpab_b200_backward(2, NC2, P, 10, 0, None, P, 1, P, 50, 0, None, None, None) == -1
+    assert L.cpab_b200_order_points(2, bad, P, 10, 1, P, P, None) == -1
+    assert L.cpab_b200_order_points(2, NC2, P, 10, 1, None, P, None) == -1
     assert L.cpab_b200_expm(5, P, 3, 0.1, P, None) == -1
     assert L.cpab_b200_project(-1, 4, 1, P, P, P, P, P, None) == -1
     assert L.cpab_b200_build_A(0, 4, 4, 1, P, P, P, P, 0.1, P, P, None) == -1
@@ -78,7 +80,7 @@ def test_other_entry_points_validate():
     zero = (ctypes.c_int64 * 2)(0, 8)
     assert L.cpab_b200_interpolate(2, P, 1, 1, zero, P, sz, P, None) == -1
     assert L.cpab_b200_interpolate_backward(2, P, 1, 1, sz, P, sz, None, P, None, None) == -1
-    assert L.cpab_b200_forward_1d_closed_form(P, 10, 0, P, 1, 0, P, None) == -1
+    assert L.cpab_b200_forward_1d_closed_form(P, 10, 0, None, P, 1, 0, P, None) == -1
 
 
 def test_errors_are_per_thread():
@@ -95,8 +97,8 @@ def test_errors_are_per_thread():
 def test_misaligned_tables_rejected():
     L = _native.lib()
     odd = ctypes.c_void_p(16 + 4)
-    assert L.cpab_b200_forward(2, NC2, P, 10, 0, P, odd, 1, 50, 0, P, None) == -1
+    assert L.cpab_b200_forward(2, NC2, P, 10, 0, None, P, odd, 1, 50, 0, P, None) == -1
     assert "aligned" in L.cpab_b200_last_error().decode()
-    assert L.cpab_b200_forward(2, NC2, P, 10, 0, odd, P, 1, 50, 0, P, None) == -1
+    assert L.cpab_b200_forward(2, NC2, P, 10, 0, None, odd, P, 1, 50, 0, P, None) == -1
     big = (ctypes.c_int32 * 2)((1 << 20) + 1, 2)
-    assert L.cpab_b200_forward(2, big, P, 10, 0, P, P, 1, 50, 0, P, None) == -1
+    assert L.cpab_b200_forward(2, big, P, 10, 0, None, P, P, 1, 50, 0, P, None) == -1
