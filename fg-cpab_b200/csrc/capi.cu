@@ -58,9 +58,6 @@ cpab::Tess make_tess(int ndim, const int32_t *nc) {
   t.fx = (float)t.nx;
   t.fy = (float)t.ny;
   t.fz = (float)t.nz;
-  t.hx = 0.5f / t.fx;
-  t.hy = 0.5f / t.fy;
-  t.hz = 0.5f / t.fz;
   return t;
 }
 

@@ -32,7 +32,6 @@ template <int ND> struct Dim {
 struct Tess {
   int nx, ny, nz;
   float fx, fy, fz;    // (float)n*
-  float hx, hy, hz;    // 0.5f / (float)n*   (3D corner rule)
 };
 
 // floor(v) for 0 <= v < 2^22, as float and int, without conversion units:
@@ -61,34 +60,37 @@ __device__ __forceinline__ int cell_of(const Tess &t, float x) {
 // comparisons are contracted to fma by nvcc; they are written as fmaf here).
 // Points strictly inside the square take a short path: there the reference's
 // lower clamp is the identity and none of its boundary branches is taken.
-static __device__ __noinline__ int cell_of_2d_outside(const Tess &t, float px, float py) {
+// (Out-of-line and given scalars, so that the caller's Tess stays in registers.)
+static __device__ __noinline__ int cell_of_2d_outside(int nx, float fnx, float fny, float px,
+                                                      float py) {
   const float xc = fminf(fmaxf(px, 0.0f), kOneMinusEps);
   const float yc = fminf(fmaxf(py, 0.0f), kOneMinusEps);
   int ix, iy;
-  const float fx0 = floor_nonneg(xc * t.fx, ix);
-  const float fy0 = floor_nonneg(yc * t.fy, iy);
-  const int base = (ix + iy * t.nx) << 2;
+  const float fx0 = floor_nonneg(xc * fnx, ix);
+  const float fy0 = floor_nonneg(yc * fny, iy);
+  const int base = (ix + iy * nx) << 2;
   if (px <= 0.0f) {
-    if (py <= 0.0f && py * t.fy < px * t.fx) return base;
-    if (py >= 1.0f && fmaf(py, t.fy, -t.fy) > -px * t.fx) return base + 2;
+    if (py <= 0.0f && py * fny < px * fnx) return base;
+    if (py >= 1.0f && fmaf(py, fny, -fny) > -px * fnx) return base + 2;
     return base + 3;
   }
   if (px >= 1.0f) {
-    if (py <= 0.0f && -py * t.fy > fmaf(px, t.fx, -t.fx)) return base;
-    if (py >= 1.0f && fmaf(py, t.fy, -t.fy) > fmaf(px, t.fx, -t.fx)) return base + 2;
+    if (py <= 0.0f && -py * fny > fmaf(px, fnx, -fnx)) return base;
+    if (py >= 1.0f && fmaf(py, fny, -fny) > fmaf(px, fnx, -fnx)) return base + 2;
     return base + 1;
   }
   if (py <= 0.0f) return base;
   if (py >= 1.0f) return base + 2;
   // Unreachable for finite inputs (handled by the caller's inside path) but
   // kept for NaN coordinates, which fail every comparison above.
-  const float lx = fmaf(xc, t.fx, -fx0);
-  const float ly = fmaf(yc, t.fy, -fy0);
+  const float lx = fmaf(xc, fnx, -fx0);
+  const float ly = fmaf(yc, fny, -fy0);
   return base + (((lx < ly) * 3) ^ ((1.0f - lx) < ly));
 }
 
 __device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
-  if (!(px > 0.0f && px < 1.0f && py > 0.0f && py < 1.0f)) return cell_of_2d_outside(t, px, py);
+  if (!(px > 0.0f && px < 1.0f && py > 0.0f && py < 1.0f))
+    return cell_of_2d_outside(t.nx, t.fx, t.fy, px, py);
   const float xc = fminf(px, kOneMinusEps);
   const float yc = fminf(py, kOneMinusEps);
   int ix, iy;
@@ -105,19 +107,19 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
 // 3D: five tetrahedra per cube (central one = 0), cube parity flips the
 // split; beyond a corner the coordinate with the smallest overshoot is moved
 // half a cell inside.  cpab/core/cpab_ops_3d.cu:67-131.
-__device__ __forceinline__ int tet_in_cube(const Tess &t, float sx, float sy, float sz) {
+__device__ __forceinline__ int tet_in_cube(int nx, int ny, int nz, float sx, float sy, float sz) {
   int i, j, k;
   float fi = floor_nonneg(sx, i);
   float fj = floor_nonneg(sy, j);
   float fk = floor_nonneg(sz, k);
   // A coordinate exactly on the upper face belongs to the last cube.
-  i = min(i, t.nx - 1); fi = fminf(fi, t.fx - 1.0f);
-  j = min(j, t.ny - 1); fj = fminf(fj, t.fy - 1.0f);
-  k = min(k, t.nz - 1); fk = fminf(fk, t.fz - 1.0f);
+  if (i > nx - 1) { i = nx - 1; fi = (float)i; }
+  if (j > ny - 1) { j = ny - 1; fj = (float)j; }
+  if (k > nz - 1) { k = nz - 1; fk = (float)k; }
   float x = sx - fi;
   float y = sy - fj;
   const float z = sz - fk;
-  const int c = 5 * (i + t.nx * (j + t.ny * k));
+  const int c = 5 * (i + nx * (j + ny * k));
   if ((i ^ j ^ k) & 1) {  // odd cubes: rotate the local frame by 90 degrees
     const float x0 = x;
     x = y;
@@ -130,29 +132,31 @@ __device__ __forceinline__ int tet_in_cube(const Tess &t, float sx, float sy, fl
   return c;
 }
 
-static __device__ __noinline__ int cell_of_3d_outside(const Tess &t, float px, float py, float pz) {
-  const float ox = (fabsf(px - 0.5f) - 0.5f) * t.fx;
-  const float oy = (fabsf(py - 0.5f) - 0.5f) * t.fy;
-  const float oz = (fabsf(pz - 0.5f) - 0.5f) * t.fz;
+static __device__ __noinline__ int cell_of_3d_outside(int nx, int ny, int nz, float px, float py,
+                                                      float pz) {
+  const float fx = (float)nx, fy = (float)ny, fz = (float)nz;
+  const float ox = (fabsf(px - 0.5f) - 0.5f) * fx;
+  const float oy = (fabsf(py - 0.5f) - 0.5f) * fy;
+  const float oz = (fabsf(pz - 0.5f) - 0.5f) * fz;
   if (ox > 0.0f && oy > 0.0f && oz > 0.0f) {
     if (ox <= oy && ox <= oz) {
-      px = (px < 0.5f) ? t.hx : 1.0f - t.hx;
+      px = (px < 0.5f) ? 0.5f / fx : 1.0f - 0.5f / fx;
     } else if (oy <= oz) {
-      py = (py < 0.5f) ? t.hy : 1.0f - t.hy;
+      py = (py < 0.5f) ? 0.5f / fy : 1.0f - 0.5f / fy;
     } else {
-      pz = (pz < 0.5f) ? t.hz : 1.0f - t.hz;
+      pz = (pz < 0.5f) ? 0.5f / fz : 1.0f - 0.5f / fz;
     }
   }
-  return tet_in_cube(t, fminf(fmaxf(px, 0.0f), 1.0f) * t.fx, fminf(fmaxf(py, 0.0f), 1.0f) * t.fy,
-                     fminf(fmaxf(pz, 0.0f), 1.0f) * t.fz);
+  return tet_in_cube(nx, ny, nz, fminf(fmaxf(px, 0.0f), 1.0f) * fx,
+                     fminf(fmaxf(py, 0.0f), 1.0f) * fy, fminf(fmaxf(pz, 0.0f), 1.0f) * fz);
 }
 
 __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
   // Inside the closed unit cube the clamps are identities and the corner rule
   // does not apply.
   if (px >= 0.0f && px <= 1.0f && py >= 0.0f && py <= 1.0f && pz >= 0.0f && pz <= 1.0f)
-    return tet_in_cube(t, px * t.fx, py * t.fy, pz * t.fz);
-  return cell_of_3d_outside(t, px, py, pz);
+    return tet_in_cube(t.nx, t.ny, t.nz, px * t.fx, py * t.fy, pz * t.fz);
+  return cell_of_3d_outside(t.nx, t.ny, t.nz, px, py, pz);
 }
 
 // ---------------------------------------------------------------------------

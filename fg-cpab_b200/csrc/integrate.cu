@@ -221,16 +221,40 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
 
-    // Phase 1: midpoint replay, keeping the start of every segment.
+    // Phase 1: midpoint replay, keeping the start of every segment and (for
+    // the plain midpoint rule) the trajectory's cell runs -- (cell, first
+    // step) each time the cell changes, ~10 per 50 steps -- so that phase 2
+    // replays a segment without cell lookups.
     float ck[kMaxSegs][ND];
+    int run_cell[ADAPT ? 1 : kMaxSteps], run_start[ADAPT ? 1 : kMaxSteps];
+    int nrun = 0, last = -1;
     for (int seg = 0; seg < nseg; ++seg) {
 #pragma unroll
       for (int k = 0; k < ND; ++k) ck[seg][k] = p[k];
       const int len = min(S, T - seg * S);
 #pragma unroll
-      for (int s = 0; s < S; ++s)
-        if (s < len) replay_step<ND, ADAPT, A_SMEM>(t, tab, p, h, h_half);
+      for (int s = 0; s < S; ++s) {
+        if (s < len) {
+          if constexpr (ADAPT) {
+            replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
+          } else {
+            const int c = lookup<ND>(t, p);
+            if (c != last) {
+              run_cell[nrun] = c;
+              run_start[nrun] = seg * S + s;
+              ++nrun;
+              last = c;
+            }
+            float m[P];
+            load_cell<ND, A_SMEM>(tab, c, m);
+            midpoint_step<ND>(m, p, h, h_half);
+          }
+        }
+      }
     }
+    // Phase-2 cursor over the runs: run r covers steps [rs, next_rs).
+    int r = nrun - 1, rs = 0;  // nrun >= 1: the first step always opens a run
+    if constexpr (!ADAPT) rs = run_start[r];
 
     // Phase 2: segments last to first; replay into registers, then walk back.
     float lam[ND];
@@ -246,12 +270,35 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
       int cs[S];
 #pragma unroll
       for (int k = 0; k < ND; ++k) p[k] = ck[seg][k];
+      // Cell of step seg*S + s for s = 0, 1, ...: start from the run r that
+      // contains the segment's first step and advance when the next run begins.
+      int j = 0, rc = 0, next_rs = 0;
+      if constexpr (!ADAPT) {
+        while (rs > seg * S) rs = run_start[--r];
+        j = r;
+        rc = run_cell[j];
+        next_rs = j + 1 < nrun ? run_start[j + 1] : T;
+      }
 #pragma unroll
       for (int s = 0; s < S; ++s) {
         if (s < len) {
 #pragma unroll
           for (int k = 0; k < ND; ++k) xs[s][k] = p[k];
-          cs[s] = replay_step<ND, ADAPT, A_SMEM>(t, tab, p, h, h_half);
+          if constexpr (ADAPT) {
+            cs[s] = replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
+          } else {
+            if (seg * S + s == next_rs) {  // the next run begins at this step
+              ++j;
+              rc = run_cell[j];
+              next_rs = j + 1 < nrun ? run_start[j + 1] : T;
+            }
+            cs[s] = rc;
+            if (s + 1 < len) {  // the segment's end point is not needed
+              float m[P];
+              load_cell<ND, A_SMEM>(tab, rc, m);
+              midpoint_step<ND>(m, p, h, h_half);
+            }
+          }
         }
       }
 #pragma unroll

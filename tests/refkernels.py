@@ -1,5 +1,9 @@
 """ctypes access to oracle/_ref/libcpab_ref.so: the reference's own CUDA
-kernels, launched as the reference launches them (test infrastructure)."""
+kernels, launched as the reference launches them (test infrastructure).
+
+The kernels run on the legacy default stream, which is torch's default
+stream; outputs are allocated with torch.zeros as the reference's launcher
+allocates them."""
 import ctypes
 import os
 
@@ -38,9 +42,7 @@ def _ncxyz(nc):
 def expm(As, dT):
     nd = As.shape[-2]
     out = torch.zeros_like(As)
-    torch.cuda.synchronize()
     assert lib().ref_expm(nd, _p(As), As.numel() // (nd * (nd + 1)), dT, _p(out)) == 0
-    torch.cuda.synchronize()
     return out
 
 
@@ -50,10 +52,8 @@ def forward(nc, points, batched, trels, As, T, adaptive):
     nP = points.shape[-1]
     out = torch.zeros((n_theta, nd, nP), device=As.device)
     nx, ny, nz = _ncxyz(nc)
-    torch.cuda.synchronize()
     assert lib().ref_forward(nd, nx, ny, nz, _p(points), nP, int(batched), _p(trels), _p(As),
                              n_theta, T, int(adaptive), _p(out)) == 0
-    torch.cuda.synchronize()
     return out
 
 
@@ -64,8 +64,6 @@ def backward(nc, points, batched, As, grad, T, adaptive):
     mom = torch.zeros((n_theta, nC, nd * (nd + 1)), device=As.device)
     gp = torch.zeros((n_theta, nd, nP), device=As.device)
     nx, ny, nz = _ncxyz(nc)
-    torch.cuda.synchronize()
     assert lib().ref_backward(nd, nx, ny, nz, nC, _p(points), nP, int(batched), _p(As), n_theta,
                               _p(grad), T, int(adaptive), _p(mom), _p(gp)) == 0
-    torch.cuda.synchronize()
     return mom, gp
