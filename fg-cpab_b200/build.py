@@ -20,7 +20,7 @@ LIB_NAME = "libcpab_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 OBJ_DIR = os.path.join(HERE, "_build")
 
-SOURCES = ["integrate.cu", "basis.cu", "resample.cu", "capi.cu"]
+SOURCES = ["integrate.cu", "basis.cu", "resample.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["cpab_device.cuh", "launch.h"]
 
 NVCC_FLAGS = [

@@ -24,6 +24,7 @@ _SIGNATURES = {
     "cpab_b200_backward": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _p, _c_int, _c_int,
                            _p, _p, _p],
     "cpab_b200_order_points": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _p],
+    "cpab_b200_order_points_static": [_c_int, _p, _p, _c_i64, _c_int, _p, _p],
     "cpab_b200_cell_index": [_c_int, _p, _p, _c_i64, _p, _p],
     "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],

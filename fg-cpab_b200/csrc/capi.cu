@@ -101,6 +101,14 @@ int check_integrate(const char *fn, int ndim, const int32_t *nc, const float *po
 
 }  // namespace
 
+int cpab::report_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 extern "C" {
 
 int cpab_b200_version(void) { return 10000; }

@@ -62,6 +62,9 @@ struct ResampleArgs {
 cudaError_t launch_interpolate(const ResampleArgs &a, cudaStream_t s);
 cudaError_t launch_interpolate_backward(const ResampleArgs &a, cudaStream_t s);
 
+// Record an error for cpab_b200_last_error() (this host thread) and return code.
+int report_error(int code, const char *fmt, ...);
+
 // Device properties cached per device (SM count, opt-in shared memory).
 struct DeviceInfo {
   int sm_count;

@@ -144,6 +144,21 @@ int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points,
                            int32_t *order, cpab_stream_t stream);
 
 /*
+ * cpab_b200_order_points without the counts_scratch argument, for callers that
+ * cannot allocate device memory (a host that only hands over the buffers it
+ * owns, code that must not risk the device-wide synchronization of
+ * cudaMalloc/cudaFree, a fixed memory budget).  The counters live in a 4 MiB
+ * array built into the library, present on every GPU that loads it; n_sets * nC
+ * may not exceed 2^20 (CPAB_ERR_SIZE otherwise).  All calls on a device share
+ * that array: calls whose GPU work overlaps race.  The first call on a device
+ * looks up the array's device address, so make it before any stream capture.
+ * No counterpart in the reference.
+ */
+int cpab_b200_order_points_static(int ndim, const int32_t *nc,
+                                  const float *points, int64_t nP, int n_sets,
+                                  int32_t *order, cpab_stream_t stream);
+
+/*
  * cells[i] = index of the tessellation cell containing points[:, i]
  * (points [ndim, n]); outside the domain, the cell the integrators use there.
  * Replaces the device lookups cuda_findcellidx_{1D,2D,3D}_fast of
