@@ -22,9 +22,7 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -82,52 +80,54 @@ def config(world):
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle-reason samples (NVML, every 5 ms) taken in a
+    background thread while the timed region runs."""
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.file = None
+        self.samples = []
+        self.stop_flag = None
+        self.thread = None
 
     def start(self):
+        import threading
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            return
+        self.stop_flag = threading.Event()
+
+        def run():
+            while not self.stop_flag.is_set():
+                try:
+                    self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                         pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:
+                    pass
+                self.stop_flag.wait(0.005)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.file.seek(0)
-        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except Exception:
-                pass
-        if not sm:
+        self.stop_flag.set()
+        self.thread.join()
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        mask = 0
+        for _, r in self.samples:
+            mask |= int(r)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for n, bit in self.REASONS.items() if mask & bit),
+                "samples": len(self.samples)}
 
 
 def init_dist():

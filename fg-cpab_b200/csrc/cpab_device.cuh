@@ -14,8 +14,9 @@
 
 namespace cpab {
 
-// Steps between adjoint checkpoints; each segment is replayed into registers.
-constexpr int kSegSteps = 8;
+// Steps between adjoint checkpoints; each segment is replayed into registers
+// (its last step is never needed, so shorter segments also replay fewer steps).
+constexpr int kSegSteps = 4;
 // Largest nstepsolver (reference: CPAB_MAX_STEPS = 100 in cpab_ops_2d.cuh:8).
 constexpr int kMaxSteps = 256;
 constexpr int kMaxSegs = kMaxSteps / kSegSteps;

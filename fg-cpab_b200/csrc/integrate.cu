@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "launch.h"
@@ -25,7 +26,12 @@ namespace cpab {
 namespace {
 
 constexpr int kFwdThreads = 512;
-constexpr int kBwdThreads = 512;
+// Backward launch shape: 2 resident blocks per SM; 3D keeps 256 threads per
+// block so that its larger per-thread state fits without spilling.
+template <int ND> struct BwdShape {
+  static constexpr int kThreads = ND == 3 ? 256 : 512;
+  static constexpr int kMinBlocks = 2;
+};
 // Shared-memory budget per block (cell table, plus the moment table in the
 // backward): two 512-thread blocks per SM give 32 resident warps.
 constexpr size_t kFwdSmemBudget = 100 * 1024;
@@ -183,8 +189,10 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
 // cpab/core/cpab_ops_3d.cu:405-532 (3D), cpab/core/cpab_ops_1d.cu:331-422 (1D).
 // ---------------------------------------------------------------------------
 
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM>
-__global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
+// CellT: type of the per-step cell record (uint16_t when nC <= 65535).
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, typename CellT>
+__global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
+    k_backward(IntegrateArgs a) {
   constexpr int P = Dim<ND>::kPpc;
   constexpr int S = kSegSteps;
   extern __shared__ float4 smem4[];
@@ -207,7 +215,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
   const float h = 1.0f / (float)T;
   const float h_half = h * 0.5f;
   const float hh = h_half * h;
-  const int nseg = (T + S - 1) / S;
+  const int nfull = T / S;         // full segments of S steps
+  const int rem = T - nfull * S;   // steps in the tail segment (0 = none)
   const int64_t nP = a.nP;
   const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
   const float *gin = a.grad_out + (int64_t)b * ND * nP;
@@ -222,39 +231,33 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
 
     // Phase 1: midpoint replay, keeping the start of every segment and (for
-    // the plain midpoint rule) the trajectory's cell runs -- (cell, first
-    // step) each time the cell changes, ~10 per 50 steps -- so that phase 2
-    // replays a segment without cell lookups.
+    // the plain midpoint rule) every step's cell, so that phase 2 replays a
+    // segment without cell lookups.  The record is 2 bytes per step for up to
+    // 65535 cells, so a thread's record stays mostly in L1.  Full segments run
+    // with compile-time trip counts; only the tail segment (T % S steps) is
+    // guarded.
     float ck[kMaxSegs][ND];
-    int run_cell[ADAPT ? 1 : kMaxSteps], run_start[ADAPT ? 1 : kMaxSteps];
-    int nrun = 0, last = -1;
-    for (int seg = 0; seg < nseg; ++seg) {
+    CellT cl[ADAPT ? 1 : kMaxSteps];
+    auto phase1 = [&](int seg, auto tail) {
+      constexpr bool kTail = decltype(tail)::value;
 #pragma unroll
       for (int k = 0; k < ND; ++k) ck[seg][k] = p[k];
-      const int len = min(S, T - seg * S);
 #pragma unroll
       for (int s = 0; s < S; ++s) {
-        if (s < len) {
-          if constexpr (ADAPT) {
-            replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
-          } else {
-            const int c = lookup<ND>(t, p);
-            if (c != last) {
-              run_cell[nrun] = c;
-              run_start[nrun] = seg * S + s;
-              ++nrun;
-              last = c;
-            }
-            float m[P];
-            load_cell<ND, A_SMEM>(tab, c, m);
-            midpoint_step<ND>(m, p, h, h_half);
-          }
+        if (kTail && s >= rem) break;
+        if constexpr (ADAPT) {
+          replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
+        } else {
+          const int c = lookup<ND>(t, p);
+          cl[seg * S + s] = (CellT)c;
+          float m[P];
+          load_cell<ND, A_SMEM>(tab, c, m);
+          midpoint_step<ND>(m, p, h, h_half);
         }
       }
-    }
-    // Phase-2 cursor over the runs: run r covers steps [rs, next_rs).
-    int r = nrun - 1, rs = 0;  // nrun >= 1: the first step always opens a run
-    if constexpr (!ADAPT) rs = run_start[r];
+    };
+    for (int seg = 0; seg < nfull; ++seg) phase1(seg, std::false_type{});
+    if (rem) phase1(nfull, std::true_type{});
 
     // Phase 2: segments last to first; replay into registers, then walk back.
     float lam[ND];
@@ -264,60 +267,47 @@ __global__ void __launch_bounds__(kBwdThreads) k_backward(IntegrateArgs a) {
 #pragma unroll
     for (int k = 0; k < P; ++k) mo[k] = 0.0f;
     int prev = -1;
-    for (int seg = nseg - 1; seg >= 0; --seg) {
-      const int len = min(S, T - seg * S);
+    auto phase2 = [&](int seg, auto tail) {
+      constexpr bool kTail = decltype(tail)::value;
       float xs[S][ND];
       int cs[S];
 #pragma unroll
       for (int k = 0; k < ND; ++k) p[k] = ck[seg][k];
-      // Cell of step seg*S + s for s = 0, 1, ...: start from the run r that
-      // contains the segment's first step and advance when the next run begins.
-      int j = 0, rc = 0, next_rs = 0;
-      if constexpr (!ADAPT) {
-        while (rs > seg * S) rs = run_start[--r];
-        j = r;
-        rc = run_cell[j];
-        next_rs = j + 1 < nrun ? run_start[j + 1] : T;
-      }
 #pragma unroll
       for (int s = 0; s < S; ++s) {
-        if (s < len) {
+        if (kTail && s >= rem) break;
 #pragma unroll
-          for (int k = 0; k < ND; ++k) xs[s][k] = p[k];
-          if constexpr (ADAPT) {
-            cs[s] = replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
-          } else {
-            if (seg * S + s == next_rs) {  // the next run begins at this step
-              ++j;
-              rc = run_cell[j];
-              next_rs = j + 1 < nrun ? run_start[j + 1] : T;
-            }
-            cs[s] = rc;
-            if (s + 1 < len) {  // the segment's end point is not needed
-              float m[P];
-              load_cell<ND, A_SMEM>(tab, rc, m);
-              midpoint_step<ND>(m, p, h, h_half);
-            }
+        for (int k = 0; k < ND; ++k) xs[s][k] = p[k];
+        if constexpr (ADAPT) {
+          cs[s] = replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
+        } else {
+          cs[s] = (int)cl[seg * S + s];
+          // The segment's end point is not needed.
+          if (kTail ? s + 1 < rem : s + 1 < S) {
+            float m[P];
+            load_cell<ND, A_SMEM>(tab, cs[s], m);
+            midpoint_step<ND>(m, p, h, h_half);
           }
         }
       }
 #pragma unroll
       for (int s = S - 1; s >= 0; --s) {
-        if (s < len) {
-          const int c = cs[s];
-          if (c != prev) {
-            if (prev >= 0) {
-              if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
-              else flush_global<P>(mom, prev, mo);
-            }
-            prev = c;
+        if (kTail && s >= rem) continue;
+        const int c = cs[s];
+        if (c != prev) {
+          if (prev >= 0) {
+            if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
+            else flush_global<P>(mom, prev, mo);
           }
-          float m[P];
-          load_cell<ND, A_SMEM>(tab, c, m);
-          adjoint_step<ND>(m, xs[s], lam, mo, h, h_half, hh);
+          prev = c;
         }
+        float m[P];
+        load_cell<ND, A_SMEM>(tab, c, m);
+        adjoint_step<ND>(m, xs[s], lam, mo, h, h_half, hh);
       }
-    }
+    };
+    if (rem) phase2(nfull, std::true_type{});
+    for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
     if (prev >= 0) {
       if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
       else flush_global<P>(mom, prev, mo);
@@ -480,15 +470,22 @@ cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
               : launch_wave(k_forward<ND, false, false>, kFwdThreads, 0, a, s);
 }
 
-template <int ND, bool ADAPT>
-cudaError_t backward_nd(const IntegrateArgs &a, cudaStream_t s) {
+template <int ND, bool ADAPT, typename CellT>
+cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
   const size_t mom = tab;
+  constexpr int kT = BwdShape<ND>::kThreads;
   if (tab + mom <= kBwdSmemBudget)
-    return launch_wave(k_backward<ND, ADAPT, true, true>, kBwdThreads, tab + mom, a, s);
+    return launch_wave(k_backward<ND, ADAPT, true, true, CellT>, kT, tab + mom, a, s);
   if (mom <= kBwdSmemBudget)
-    return launch_wave(k_backward<ND, ADAPT, false, true>, kBwdThreads, mom, a, s);
-  return launch_wave(k_backward<ND, ADAPT, false, false>, kBwdThreads, 0, a, s);
+    return launch_wave(k_backward<ND, ADAPT, false, true, CellT>, kT, mom, a, s);
+  return launch_wave(k_backward<ND, ADAPT, false, false, CellT>, kT, 0, a, s);
+}
+
+template <int ND, bool ADAPT>
+cudaError_t backward_nd(const IntegrateArgs &a, cudaStream_t s) {
+  if (ADAPT || a.nC <= 65535) return backward_cells<ND, ADAPT, uint16_t>(a, s);
+  return backward_cells<ND, ADAPT, int32_t>(a, s);
 }
 
 }  // namespace
