@@ -173,10 +173,18 @@ def cpu_sample_points(O, basis, theta, target_s):
     return max(1024, min(N_POINTS, n))
 
 
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(basis, theta_np, target_s=10.0):
     """The oracle port on all host threads: repeated fwd+grad steps on (a
     sample of) the workload until about target_s seconds have passed."""
     from oracle import oracle as O
+    O.set_num_threads(host_threads())   # torchrun sets OMP_NUM_THREADS=1
     n = cpu_sample_points(O, basis, theta_np, target_s)
     pts = np.random.default_rng(1).random((2, n), dtype=np.float32)
     reps, t0 = 0, time.perf_counter()
@@ -196,6 +204,7 @@ def run_reference(args, rank, world):
         return
     from cpab import Cpab
     from oracle import oracle as O
+    O.set_num_threads(host_threads())   # torchrun sets OMP_NUM_THREADS=1
     C = Cpab(TESS, zero_boundary=True)
     theta = torch.randn(BATCH, C.params.d, generator=torch.Generator().manual_seed(0)).numpy()
     n = cpu_sample_points(O, C.params.basis, theta, 3.0)
@@ -211,12 +220,12 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config(1), "impl": "reference",
+        "config": config(world), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
                          "sample": "%d of %d points x batch %d per step" % (n, N_POINTS, BATCH)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -372,10 +381,26 @@ def run_ours(args, rank, world, local):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(C.params.basis, theta_h.numpy())
-        print(json.dumps(line), flush=True)
+        emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line):
+    """Print the result line on the real stdout (everything else, including
+    what NCCL or CUDA libraries print, goes to stderr)."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)            # stdout of this process (and its libraries) -> stderr
+    sys.stdout = sys.stderr
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -383,12 +408,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.impl == "reference":
+        # CPU only: no process group; under torchrun rank 0 alone runs it.
+        run_reference(args, int(os.environ.get("RANK", "0")),
+                      int(os.environ.get("WORLD_SIZE", "1")))
+        return
     rank, world, local = init_dist()
     try:
-        if args.impl == "reference":
-            run_reference(args, rank, world)
-        else:
-            run_ours(args, rank, world, local)
+        run_ours(args, rank, world, local)
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
