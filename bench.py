@@ -232,26 +232,116 @@ def run_reference(args, rank, world):
 # GPU arm.
 # ---------------------------------------------------------------------------
 
-def run_ours(args, rank, world, local):
-    from cpab import Cpab, _native
-    from cpab.distributed import transform_grid_sharded
+class Workload:
+    """One benchmark configuration: inputs, one fwd+grad step, work counted."""
 
-    dev = torch.device("cuda", local)
-    C = Cpab(TESS, zero_boundary=True)
-    d = C.params.d
-    theta_h = torch.randn(BATCH, d, generator=torch.Generator().manual_seed(0))
-    pts_h = torch.rand(2, N_POINTS, generator=torch.Generator().manual_seed(1 + rank))
+    def __init__(self, name, desc, tess, zero_boundary, batch, stages, scaling, parallelism):
+        self.name, self.desc = name, desc
+        self.tess, self.zero_boundary = tess, zero_boundary
+        self.batch, self.stages = batch, stages
+        self.scaling, self.parallelism = scaling, parallelism
+
+
+def make_workload(name, rank, world, dev):
+    """Build (workload, host inputs, step function, pairs per step on this rank)."""
+    from cpab import Cpab
+    from cpab.distributed import allreduce_theta_grad, shard_points, transform_grid_sharded
+    gen = lambda seed: torch.Generator().manual_seed(seed)  # noqa: E731
     group = dist.group.WORLD if world > 1 else None
 
-    def fwd_grad(pts, theta):
-        t = theta.detach().requires_grad_(True)
-        if group is None:
-            out = C.transform_grid(pts, t)
+    if name in ("2d", "2d12", "2d30", "1d"):
+        tess = {"2d": [20, 20], "2d12": [12, 12], "2d30": [30, 30], "1d": [50]}[name]
+        nd = len(tess)
+        B, nP = (8, 100_000) if nd == 1 else (BATCH, N_POINTS)
+        w = Workload(name, "%dD Cpab(%s, zero_boundary=True): batch %d, %d U[0,1]^%d points per GPU, "
+                     "theta~N(0,1), nstepsolver 50; transform_grid + %s + backward to theta"
+                     % (nd, tess, B, nP, nd, "sum((x_t-x)^2)" if nd == 1 else "MSE(x_t, x)"),
+                     tess, True, B, 1, "weak", "points sharded over %d GPU(s), dtheta allreduce" % world)
+        C = Cpab(tess, zero_boundary=True)
+        host = {"theta": torch.randn(B, C.params.d, generator=gen(0)),
+                "points": torch.rand(nd, nP, generator=gen(1 + rank))}
+
+        def step(x):
+            t = x["theta"].requires_grad_(True)
+            pts = x["points"]
+            out = C.transform_grid(pts, t) if group is None else transform_grid_sharded(C, pts, t, group)
+            loss = ((out - pts) ** 2).sum() if nd == 1 else ((out - pts) ** 2).mean()
+            loss.backward()
+            return loss, t.grad
+        return w, C, host, step, B * nP
+
+    if name in ("dense2d", "3d"):
+        if name == "dense2d":
+            tess, zb, B, shape, scale = [30, 30], False, 32, [3, 512, 512], 0.5
         else:
-            out = transform_grid_sharded(C, pts, t, group)
-        loss = ((out - pts) ** 2).mean()
-        loss.backward()
-        return loss, t.grad
+            tess, zb, B, shape, scale = [10, 10, 10], True, 4, [1, 128, 128, 128], 1.0
+        nd = len(tess)
+        w = Workload(name, "%dD Cpab(%s, zero_boundary=%s): transform_data of %d x %s, theta~N(0,%g^2), "
+                     "MSE to a second %s, backward to theta; each GPU its own batch"
+                     % (nd, tess, zb, B, shape, scale, "image" if nd == 2 else "volume"),
+                     tess, zb, B, 1, "weak", "batch-parallel over %d GPU(s), no collective" % world)
+        C = Cpab(tess, zero_boundary=zb)
+        g = gen(2 + 10 * rank)
+        if nd == 2:
+            data = torch.rand(B, *shape, generator=g)
+            target = torch.rand(B, *shape, generator=g)
+        else:
+            data = torch.stack([blobs(shape[1:], g) for _ in range(B)])[:, None]
+            target = torch.stack([blobs(shape[1:], g) for _ in range(B)])[:, None]
+        host = {"theta": torch.randn(B, C.params.d, generator=gen(0)) * scale, "data": data,
+                "target": target}
+        outsize = shape[1:]
+
+        def step(x):
+            t = x["theta"].requires_grad_(True)
+            out = C.transform_data(x["data"], t, outsize)
+            loss = ((out - x["target"]) ** 2).mean()
+            loss.backward()
+            return loss, t.grad
+        return w, C, host, step, B * int(np.prod(outsize))
+
+    if name == "chain3d":
+        tess, K, grid_n = [16, 16, 16], 4, [160, 192, 160]
+        w = Workload(name, "3D Cpab([16,16,16], zero_boundary=True): transform_grid_chain, 4 stages, "
+                     "scale_by_dt, theta_chain~N(0,0.5^2), 160x192x160 meshgrid (4,915,200 points) "
+                     "sharded over the GPUs, sum((x_t-x)^2) + backward to theta_chain",
+                     tess, True, 1, K, "strong",
+                     "meshgrid sharded over %d GPU(s), one dtheta allreduce" % world)
+        C = Cpab(tess, zero_boundary=True)
+        grid = shard_points(C.uniform_meshgrid(grid_n, device="cpu"), rank, world)
+        host = {"theta": torch.randn(K, C.params.d, generator=gen(0)) * 0.5, "points": grid}
+
+        def step(x):
+            t = x["theta"].requires_grad_(True)
+            if group is not None:
+                allreduce_theta_grad(t, group)
+            out = C.transform_grid_chain(x["points"], t, scale_by_dt=True)
+            loss = ((out - x["points"]) ** 2).sum()
+            loss.backward()
+            return loss, t.grad
+        return w, C, host, step, grid.shape[1] * K
+    raise ValueError("unknown config " + name)
+
+
+def blobs(shape, g, n=20):
+    """Sum of n Gaussian blobs (sigma ~ U[4,16] voxels, centres ~ U over the
+    volume, unit amplitude) on a grid of the given shape."""
+    axes = [torch.arange(s, dtype=torch.float32) for s in shape]
+    zz, yy, xx = torch.meshgrid(*axes, indexing="ij")
+    vol = torch.zeros(shape)
+    for _ in range(n):
+        c = [torch.rand(1, generator=g).item() * s for s in shape]
+        sig = 4 + 12 * torch.rand(1, generator=g).item()
+        vol += torch.exp(-((zz - c[0]) ** 2 + (yy - c[1]) ** 2 + (xx - c[2]) ** 2) / (2 * sig * sig))
+    return vol
+
+
+def run_ours(args, rank, world, local):
+    from cpab import _native
+
+    dev = torch.device("cuda", local)
+    w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev)
+    default = args.config == "2d"
 
     # Per-launch timing of the integration kernels, on the stream they run on.
     timings = {"forward": [], "backward": []}
@@ -270,11 +360,14 @@ def run_ours(args, rank, world, local):
 
     _native.forward, _native.backward = timed("forward"), timed("backward")
 
-    pts = pts_h.to(dev)
-    theta = theta_h.to(dev)
+    resident = {k: v.to(dev) for k, v in host.items()}
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+
+    def dev_step():
+        return step(dict(resident, theta=resident["theta"].detach()))
+
     for _ in range(args.warmup):
-        fwd_grad(pts, theta)
+        dev_step()
     torch.cuda.synchronize()
 
     clocks = Clocks(local)
@@ -289,7 +382,7 @@ def run_ours(args, rank, world, local):
         flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        fwd_grad(pts, theta)
+        dev_step()
         e.record()
         ev.append((s, e))
     torch.cuda.synchronize()
@@ -300,24 +393,23 @@ def run_ours(args, rank, world, local):
     total_ms = sum(s.elapsed_time(e) for s, e in ev)
     kern = {k: sum(s.elapsed_time(e) for s, e in v) / max(len(v), 1) for k, v in timings.items()
             if k != "on"}
+    launches = {k: len(v) // max(args.steps, 1) for k, v in timings.items() if k != "on"}
     total_ms = max_over_ranks(total_ms, world)
     kern = {k: max_over_ranks(v, world) for k, v in kern.items()}
     ms_step = total_ms / args.steps
-    pairs_step = BATCH * N_POINTS * world
+    pairs_step = pairs_rank * world
     value = pairs_step / (ms_step * 1e-3)
 
     # End to end: pinned host inputs in, loss and gradient out, every step.
-    pts_pin = pts_h.pin_memory()
-    th_pin = theta_h.pin_memory()
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    on_dev = {k: torch.empty_like(v) for k, v in resident.items()}
     loss_pin = torch.empty(1, pin_memory=True)
-    grad_pin = torch.empty(BATCH, d, pin_memory=True)
-    pts_d = torch.empty_like(pts)
-    th_d = torch.empty_like(theta)
+    grad_pin = torch.empty_like(host["theta"]).pin_memory()
 
     def e2e_step():
-        pts_d.copy_(pts_pin, non_blocking=True)
-        th_d.copy_(th_pin, non_blocking=True)
-        loss, grad = fwd_grad(pts_d, th_d)
+        for k in pinned:
+            on_dev[k].copy_(pinned[k], non_blocking=True)
+        loss, grad = step(dict(on_dev, theta=on_dev["theta"].detach()))
         loss_pin.copy_(loss.detach().reshape(1), non_blocking=True)
         grad_pin.copy_(grad, non_blocking=True)
 
@@ -338,35 +430,42 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.barrier()
     e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world) / args.steps
-    h2d = pts_h.numel() * 4 + theta_h.numel() * 4
-    d2h = 4 + theta_h.numel() * 4
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = 4 + host["theta"].numel() * 4
 
     if rank == 0:
         hbm, peak_kind = peaks()
-        nC = C.params.nC
-        # Algorithmic bytes of one backward launch: points (shared by the
-        # batch), upstream gradient, cell matrices in, moments out.
-        bwd_bytes = (2 * N_POINTS + BATCH * 2 * N_POINTS + 2 * BATCH * nC * 6) * 4
+        p = C.params
+        nd, ppc = p.ndim, p.params_pr_cell
+        # Algorithmic bytes of one backward launch: the points, the upstream
+        # gradient, cell matrices in and moments out (per stage).
+        pts_per_launch = pairs_rank // (w.batch * w.stages)
+        bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
+                     + 2 * w.batch * p.nC * ppc) * 4
         ach = bwd_bytes / (kern["backward"] * 1e-3) / 1e9
-        traffic = profiled("traffic_bytes_per_launch")
-        # The kernel is bound by instruction issue (4 schedulers x 148 SMs, one
-        # warp instruction per scheduler per clock); the profiled instruction
-        # count over the live launch time gives its issue-rate fraction.
-        inst = profiled("warp_instructions_per_launch")
+        traffic = profiled("traffic_bytes_per_launch") if default else None
+        inst = profiled("warp_instructions_per_launch") if default else None
         clk_mhz = (clk or {}).get("sm_mhz") or 1965.0
         issue_peak = 4 * 148 * clk_mhz * 1e6
         issue = None
         if inst:
+            # The kernel is bound by instruction issue (4 schedulers x 148 SMs,
+            # one warp instruction per scheduler per clock); the profiled
+            # instruction count over the live launch time gives its fraction.
             issue_ach = inst / (kern["backward"] * 1e-3)
             issue = {"bound": "issue", "achieved": issue_ach, "peak": issue_peak,
                      "unit": "warp-inst/s", "frac": issue_ach / issue_peak,
                      "inst_per_launch": inst, "sm_mhz": clk_mhz,
                      "source": "profiles/k_backward_2d_20x20_b16_125k.md"}
+        cfg = config(world) if default else {
+            "workload": w.desc, "tess": w.tess, "batch": w.batch, "stages": w.stages,
+            "nstepsolver": NSTEP, "global_batch": pairs_step, "parallelism": w.parallelism,
+            "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20)}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config(world),
+            "scaling": w.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": cfg,
             "e2e": {"value": pairs_step / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "kernel": "k_backward (fused adjoint)",
@@ -375,12 +474,12 @@ def run_ours(args, rank, world, local):
                          "algorithmic_bytes_per_launch": bwd_bytes},
             "issue_roofline": issue,
             "kernel_ms": kern,
-            # per step: build_A, histogram, scan, scatter, forward, backward, project
-            "gpu_launches": 7 * args.steps,
+            # per transform: build_A, histogram, scan, scatter, forward, backward, project
+            "gpu_launches": 7 * launches["backward"] * args.steps,
             "clocks": clk,
         }
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(C.params.basis, theta_h.numpy())
+        if default and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(C.params.basis, host["theta"].numpy())
         emit(line)
 
 
@@ -407,6 +506,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="2d",
+                    choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d"],
+                    help="workload (default: BASELINE configs[1], 2D 20x20)")
     args = ap.parse_args()
     if args.impl == "reference":
         # CPU only: no process group; under torchrun rank 0 alone runs it.

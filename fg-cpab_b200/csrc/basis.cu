@@ -3,10 +3,9 @@
 // dtheta = B^T vec(M).
 //
 // These are small sparse contractions (a handful of nonzeros per row for
-// zero-boundary bases) -- gathers, not GEMMs -- so they run on the SIMT
-// pipes: one thread per (transformation, cell) for the A-build, one thread
-// per (transformation, basis column) for the projection with the
-// transformation index fastest so that CSR index/value loads are broadcast.
+// zero-boundary bases, dozens for general ones) -- gathers, not GEMMs -- so
+// they run on the SIMT pipes, one warp per cell (A-build) or per basis column
+// (projection) with the nonzeros split over the lanes.
 #include <cuda_runtime.h>
 
 #include "launch.h"
@@ -228,51 +227,84 @@ __global__ void k_expm(const float *__restrict__ As, int64_t n, float dT, float 
   for (int k = 0; k < P; ++k) trels[i * P + k] = r[k];
 }
 
-// One thread per (transformation, cell): the cell's kPpc rows of B dotted with
-// theta, then (optionally) the cell's matrix exponential.
+// One warp per cell.  For each transformation t the warp forms the cell's kPpc
+// entries A[t, c, r] = sum_k B[r, k] theta[t, k]: the row's nonzeros are split
+// over the lanes and summed with a butterfly (the column indices of a row are
+// clustered, so the lanes' theta loads share sectors).  Lane t keeps
+// transformation t's entries and then computes that cell's exponential, so
+// the expm work runs 32 transformations wide.  Rows of a zero-boundary basis
+// have <= 4 nonzeros; general bases have dozens.
 template <int ND>
-__global__ void k_build_A(int64_t nC, int64_t d, int n_theta, const int32_t *__restrict__ rowptr,
-                          const int32_t *__restrict__ colidx, const float *__restrict__ vals,
-                          const float *__restrict__ theta, float dT, float *__restrict__ As,
-                          float *__restrict__ trels) {
+__global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_theta,
+                                                 const int32_t *__restrict__ rowptr,
+                                                 const int32_t *__restrict__ colidx,
+                                                 const float *__restrict__ vals,
+                                                 const float *__restrict__ theta, float dT,
+                                                 float *__restrict__ As,
+                                                 float *__restrict__ trels) {
   constexpr int P = Dim<ND>::kPpc;
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= nC * n_theta) return;
-  const int64_t t = i / nC;
-  const int64_t c = i - t * nC;
-  const float *th = theta + t * d;
-  float a[P];
+  const int64_t c = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (c >= nC) return;  // whole warps exit together
+  int k0[P], k1[P];
 #pragma unroll
   for (int r = 0; r < P; ++r) {
-    const int64_t row = c * P + r;
-    const int k0 = __ldg(rowptr + row), k1 = __ldg(rowptr + row + 1);
-    float s = 0.0f;
-    for (int k = k0; k < k1; ++k) s = fmaf(__ldg(vals + k), __ldg(th + __ldg(colidx + k)), s);
-    a[r] = s;
+    k0[r] = __ldg(rowptr + c * P + r);
+    k1[r] = __ldg(rowptr + c * P + r + 1);
   }
+  for (int t0 = 0; t0 < n_theta; t0 += 32) {
+    float mine[P];  // entries of transformation t0 + lane
 #pragma unroll
-  for (int r = 0; r < P; ++r) As[i * P + r] = a[r];
-  if (trels != nullptr) {
-    float e[P];
-    expm_cell<ND>(a, dT, e);
+    for (int r = 0; r < P; ++r) mine[r] = 0.0f;
+    const int tn = min(32, n_theta - t0);
+    for (int j = 0; j < tn; ++j) {
+      const float *th = theta + (int64_t)(t0 + j) * d;
 #pragma unroll
-    for (int r = 0; r < P; ++r) trels[i * P + r] = e[r];
+      for (int r = 0; r < P; ++r) {
+        float sum = 0.0f;
+        for (int k = k0[r] + lane; k < k1[r]; k += 32)
+          sum = fmaf(__ldg(vals + k), __ldg(th + __ldg(colidx + k)), sum);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (lane == j) mine[r] = sum;
+      }
+    }
+    if (lane < tn) {
+      const int64_t base = ((int64_t)(t0 + lane) * nC + c) * P;
+#pragma unroll
+      for (int r = 0; r < P; ++r) As[base + r] = mine[r];
+      if (trels != nullptr) {
+        float e[P];
+        expm_cell<ND>(mine, dT, e);
+#pragma unroll
+        for (int r = 0; r < P; ++r) trels[base + r] = e[r];
+      }
+    }
   }
 }
 
-// dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].
-__global__ void k_project(int64_t d, int64_t D, int n_theta, const int32_t *__restrict__ rowptr,
-                          const int32_t *__restrict__ colidx, const float *__restrict__ vals,
-                          const float *__restrict__ moments, float *__restrict__ dtheta) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= d * n_theta) return;
-  const int64_t j = i / n_theta;
-  const int64_t t = i - j * n_theta;
-  const float *m = moments + t * D;
+// dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].  One warp
+// per basis column j: the lanes split the row's nonzeros (clustered column
+// indices, so the moment gathers share sectors) and a butterfly sums each
+// transformation's dot product.
+__global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_theta,
+                                                 const int32_t *__restrict__ rowptr,
+                                                 const int32_t *__restrict__ colidx,
+                                                 const float *__restrict__ vals,
+                                                 const float *__restrict__ moments,
+                                                 float *__restrict__ dtheta) {
+  const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= d) return;
   const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
-  float s = 0.0f;
-  for (int k = k0; k < k1; ++k) s = fmaf(__ldg(vals + k), __ldg(m + __ldg(colidx + k)), s);
-  dtheta[t * d + j] = s;
+  for (int t = 0; t < n_theta; ++t) {
+    const float *m = moments + (int64_t)t * D;
+    float sum = 0.0f;
+    for (int k = k0 + lane; k < k1; k += 32) sum = fmaf(__ldg(vals + k), __ldg(m + __ldg(colidx + k)), sum);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) dtheta[(int64_t)t * d + j] = sum;
+  }
 }
 
 constexpr int kThreads = 256;
@@ -295,8 +327,8 @@ cudaError_t launch_expm(int ndim, const float *As, int64_t n, float dT, float *t
 cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_t *rowptr,
                            const int32_t *colidx, const float *vals, const float *theta,
                            float dT, float *As, float *trels, cudaStream_t s) {
-  const int64_t n = nC * n_theta;
-  if (n == 0) return cudaSuccess;
+  if (nC * n_theta == 0) return cudaSuccess;
+  const int64_t n = nC * 32;  // one warp per cell
   switch (ndim) {
     case 1:
       k_build_A<1><<<blocks_for(n), kThreads, 0, s>>>(nC, d, n_theta, rowptr, colidx, vals, theta,
@@ -317,8 +349,8 @@ cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const i
 cudaError_t launch_project(int64_t d, int64_t D, int n_theta, const int32_t *rowptr,
                            const int32_t *colidx, const float *vals, const float *moments,
                            float *dtheta, cudaStream_t s) {
-  const int64_t n = d * n_theta;
-  if (n == 0) return cudaSuccess;
+  if (d * n_theta == 0) return cudaSuccess;
+  const int64_t n = d * 32;  // one warp per basis column
   k_project<<<blocks_for(n), kThreads, 0, s>>>(d, D, n_theta, rowptr, colidx, vals, moments,
                                                dtheta);
   return cudaGetLastError();

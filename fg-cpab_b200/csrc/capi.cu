@@ -184,6 +184,7 @@ int cpab_b200_backward(int ndim, const int32_t *nc, const float *points, int64_t
   if (st != CPAB_OK) return st;
   if (n_theta == 0) return ok();
   if (moments == nullptr) return fail(CPAB_ERR_ARG, "backward: null moments");
+  if (!aligned16(moments)) return fail(CPAB_ERR_ARG, "backward: moments must be 16-byte aligned");
   if (nP > 0 && grad_out == nullptr) return fail(CPAB_ERR_ARG, "backward: null grad_out");
   const size_t mbytes = (size_t)n_theta * a.nC * ndim * (ndim + 1) * sizeof(float);
   cudaError_t e = cudaMemsetAsync(moments, 0, mbytes, stream);
@@ -254,6 +255,10 @@ int check_resample(const char *fn, int ndim, const float *data, int n_batch, int
     P *= out_size[k];
   }
   if (n_batch > 65535) return fail(CPAB_ERR_SIZE, "%s: batch larger than 65535", fn);
+  int64_t plane = 1;
+  for (int k = 0; k < ndim; ++k) plane *= in_size[k];
+  if (plane >= ((int64_t)1 << 31))
+    return fail(CPAB_ERR_SIZE, "%s: one input channel has 2^31 or more elements", fn);
   if (ndim >= 2 && (out_size[0] + 31) / 32 > 65535)
     return fail(CPAB_ERR_SIZE, "%s: output axis 0 too long", fn);
   if (ndim == 3 && (int64_t)n_batch * out_size[1] > 65535)

@@ -82,26 +82,30 @@ static __device__ __noinline__ int cell_of_2d_outside(int nx, float fnx, float f
   }
   if (py <= 0.0f) return base;
   if (py >= 1.0f) return base + 2;
-  // Unreachable for finite inputs (handled by the caller's inside path) but
-  // kept for NaN coordinates, which fail every comparison above.
+  // Inside the square: points within 1e-7 of the upper faces (the caller's
+  // short path excludes them) and NaN coordinates, which fail every
+  // comparison above.
   const float lx = fmaf(xc, fnx, -fx0);
   const float ly = fmaf(yc, fny, -fy0);
   return base + (((lx < ly) * 3) ^ ((1.0f - lx) < ly));
 }
 
 __device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
-  if (!(px > 0.0f && px < 1.0f && py > 0.0f && py < 1.0f))
+  // Inside (0, 1 - 1e-7) the reference's clamp is the identity; the few
+  // points in [1 - 1e-7, 1) take the general path, which clamps them.
+  if (!(px > 0.0f && px < kOneMinusEps && py > 0.0f && py < kOneMinusEps))
     return cell_of_2d_outside(t.nx, t.fx, t.fy, px, py);
-  const float xc = fminf(px, kOneMinusEps);
-  const float yc = fminf(py, kOneMinusEps);
-  int ix, iy;
-  // xc * n < n for every n < 2^24 because xc <= 1 - 2^-23: no upper clamp.
-  const float fx0 = floor_nonneg(xc * t.fx, ix);
-  const float fy0 = floor_nonneg(yc * t.fy, iy);
-  const float lx = fmaf(xc, t.fx, -fx0);
-  const float ly = fmaf(yc, t.fy, -fy0);
-  const int upper_left = lx < ly;           // above the main diagonal
-  const int upper_right = (1.0f - lx) < ly;  // above the anti-diagonal
+  // px * n < n for every n < 2^24 because px < 1 - 2^-23: no upper clamp.
+  // floor_nonneg on both coordinates at once (paired fp32 instructions):
+  // r = 2^23 + floor(p * n), -floor = 2^23 - r (exact), l = fma(p, n, -floor).
+  const float2 p = make_float2(px, py), n = make_float2(t.fx, t.fy);
+  const float2 k23 = make_float2(8388608.0f, 8388608.0f);
+  const float2 r = __fadd2_rd(__fmul2_rn(p, n), k23);
+  const float2 l = __ffma2_rn(p, n, __ffma2_rn(r, make_float2(-1.0f, -1.0f), k23));
+  const int ix = __float_as_int(r.x) - 0x4B000000;
+  const int iy = __float_as_int(r.y) - 0x4B000000;
+  const int upper_left = l.x < l.y;            // above the main diagonal
+  const int upper_right = (1.0f - l.x) < l.y;  // above the anti-diagonal
   return ((ix + iy * t.nx) << 2) + ((upper_left * 3) ^ upper_right);
 }
 
@@ -152,19 +156,45 @@ static __device__ __noinline__ int cell_of_3d_outside(int nx, int ny, int nz, fl
                      fminf(fmaxf(py, 0.0f), 1.0f) * fy, fminf(fmaxf(pz, 0.0f), 1.0f) * fz);
 }
 
+// Tetrahedron of a point with 0 <= s* < n* (cube coordinates): no clamping.
+__device__ __forceinline__ int tet_in_cube_inside(int nx, int ny, float sx, float sy, float sz) {
+  int i, j, k;
+  const float fi = floor_nonneg(sx, i);
+  const float fj = floor_nonneg(sy, j);
+  const float fk = floor_nonneg(sz, k);
+  float x = sx - fi;
+  float y = sy - fj;
+  const float z = sz - fk;
+  const int c = 5 * (i + nx * (j + ny * k));
+  if ((i ^ j ^ k) & 1) {
+    const float x0 = x;
+    x = y;
+    y = 1.0f - x0;
+  }
+  if (-x - y + z >= 0.0f) return c + 1;
+  if (x + y + z - 2.0f >= 0.0f) return c + 2;
+  if (-x + y - z >= 0.0f) return c + 3;
+  if (x - y - z >= 0.0f) return c + 4;
+  return c;
+}
+
 __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
-  // Inside the closed unit cube the clamps are identities and the corner rule
-  // does not apply.
-  if (px >= 0.0f && px <= 1.0f && py >= 0.0f && py <= 1.0f && pz >= 0.0f && pz <= 1.0f)
-    return tet_in_cube(t.nx, t.ny, t.nz, px * t.fx, py * t.fy, pz * t.fz);
+  // In [0, 1) the reference's clamps are identities, the corner rule does not
+  // apply, and p * n rounds below n, so floor(p * n) <= n - 1 needs no clamp;
+  // everything else (including coordinates exactly 1) takes the general path.
+  if (px >= 0.0f && px < 1.0f && py >= 0.0f && py < 1.0f && pz >= 0.0f && pz < 1.0f)
+    return tet_in_cube_inside(t.nx, t.ny, px * t.fx, py * t.fy, pz * t.fz);
   return cell_of_3d_outside(t.nx, t.ny, t.nz, px, py, pz);
 }
 
 // ---------------------------------------------------------------------------
-// Cell tables: kPpc floats per cell, rows packed back to back (the layout of
-// the reference's As/Trels).  A 2D row is 24 bytes and loads as three 64-bit
-// words; a 3D row is 48 bytes, three 128-bit words.  Packed rows spread
-// neighbouring cells over distinct shared-memory banks.
+// Cell tables: kPpc floats per cell, rows packed back to back.  In global
+// memory this is the reference's As/Trels layout (row-major ND x (ND+1)).  A
+// 2D table staged in shared memory is stored by column pairs instead --
+// (m00, m10), (m01, m11), (m02, m12) -- so that both rows of a step are
+// evaluated with paired fp32 instructions; it is still 24 bytes a cell, three
+// 64-bit words.  A 3D row is 48 bytes, three 128-bit words.  Packed rows
+// spread neighbouring cells over distinct shared-memory banks.
 // ---------------------------------------------------------------------------
 
 template <int ND, bool SMEM>
@@ -176,9 +206,13 @@ __device__ __forceinline__ void load_cell(const float *__restrict__ tab, int c,
     m[0] = v.x; m[1] = v.y;
   } else if constexpr (ND == 2) {
     const float2 *p = reinterpret_cast<const float2 *>(tab) + 3 * c;
-    const float2 u = SMEM ? p[0] : __ldg(p), v = SMEM ? p[1] : __ldg(p + 1),
-                 w = SMEM ? p[2] : __ldg(p + 2);
-    m[0] = u.x; m[1] = u.y; m[2] = v.x; m[3] = v.y; m[4] = w.x; m[5] = w.y;
+    if constexpr (SMEM) {  // column pairs
+      const float2 c0 = p[0], c1 = p[1], c2 = p[2];
+      m[0] = c0.x; m[1] = c1.x; m[2] = c2.x; m[3] = c0.y; m[4] = c1.y; m[5] = c2.y;
+    } else {
+      const float2 u = __ldg(p), v = __ldg(p + 1), w = __ldg(p + 2);
+      m[0] = u.x; m[1] = u.y; m[2] = v.x; m[3] = v.y; m[4] = w.x; m[5] = w.y;
+    }
   } else {
     const float4 *p = reinterpret_cast<const float4 *>(tab) + 3 * c;
     const float4 u = SMEM ? p[0] : __ldg(p);
@@ -190,12 +224,24 @@ __device__ __forceinline__ void load_cell(const float *__restrict__ tab, int c,
   }
 }
 
-// Copy n floats (a multiple of 2, 8-byte aligned) from global to shared memory.
+// Stage the nC-cell table g (global, reference layout, 8-byte aligned) into
+// shared memory s; 2D tables are transposed into column pairs on the way.
+template <int ND>
 __device__ __forceinline__ void stage_table(float *__restrict__ s, const float *__restrict__ g,
-                                            int n) {
+                                            int nC) {
   const float2 *g2 = reinterpret_cast<const float2 *>(g);
   float2 *s2 = reinterpret_cast<float2 *>(s);
-  for (int i = threadIdx.x; i < n / 2; i += blockDim.x) s2[i] = __ldg(g2 + i);
+  if constexpr (ND == 2) {
+    for (int c = threadIdx.x; c < nC; c += blockDim.x) {
+      const float2 u = __ldg(g2 + 3 * c), v = __ldg(g2 + 3 * c + 1), w = __ldg(g2 + 3 * c + 2);
+      s2[3 * c] = make_float2(u.x, v.y);
+      s2[3 * c + 1] = make_float2(u.y, w.x);
+      s2[3 * c + 2] = make_float2(v.x, w.y);
+    }
+  } else {
+    const int n = nC * Dim<ND>::kPpc / 2;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s2[i] = __ldg(g2 + i);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -204,9 +250,23 @@ __device__ __forceinline__ void stage_table(float *__restrict__ s, const float *
 // column inwards.
 // ---------------------------------------------------------------------------
 
+// Two fp32 lanes x, y -> one float2 (and back): the paired instructions of
+// sm_100 (FFMA2/FMUL2/FADD2) round every component exactly as their scalar
+// counterparts, so the 2D steps below are bit-identical to the scalar
+// sequence while issuing half as many floating-point instructions.
+__device__ __forceinline__ float2 bc(float x) { return make_float2(x, x); }
+
 template <int ND>
 __device__ __forceinline__ void affine(const float (&m)[Dim<ND>::kPpc], const float (&p)[ND],
                                        float (&v)[ND]) {
+  if constexpr (ND == 2) {
+    const float2 c0 = make_float2(m[0], m[3]), c1 = make_float2(m[1], m[4]),
+                 c2 = make_float2(m[2], m[5]);
+    const float2 r = __ffma2_rn(c0, bc(p[0]), __ffma2_rn(c1, bc(p[1]), c2));
+    v[0] = r.x;
+    v[1] = r.y;
+    return;
+  }
 #pragma unroll
   for (int r = 0; r < ND; ++r) {
     const float *row = m + r * (ND + 1);
@@ -229,6 +289,18 @@ __device__ __forceinline__ int lookup(const Tess &t, const float (&p)[ND]) {
 template <int ND>
 __device__ __forceinline__ void midpoint_step(const float (&m)[Dim<ND>::kPpc], float (&p)[ND],
                                               float h, float h_half) {
+  if constexpr (ND == 2) {
+    const float2 c0 = make_float2(m[0], m[3]), c1 = make_float2(m[1], m[4]),
+                 c2 = make_float2(m[2], m[5]);
+    const float2 x = make_float2(p[0], p[1]);
+    const float2 v = __ffma2_rn(c0, bc(x.x), __ffma2_rn(c1, bc(x.y), c2));
+    const float2 q = __ffma2_rn(bc(h_half), v, x);
+    const float2 w = __ffma2_rn(c0, bc(q.x), __ffma2_rn(c1, bc(q.y), c2));
+    const float2 y = __ffma2_rn(bc(h), w, x);
+    p[0] = y.x;
+    p[1] = y.y;
+    return;
+  }
   float v[ND], q[ND], w[ND];
   affine<ND>(m, p, v);
 #pragma unroll
@@ -280,6 +352,35 @@ __device__ __forceinline__ void adjoint_step(const float (&m)[Dim<ND>::kPpc], co
                                              float (&lam)[ND], float (&mo)[Dim<ND>::kPpc],
                                              float h, float h_half, float hh) {
   constexpr int C = ND + 1;
+  if constexpr (ND == 2) {
+    // Moment pairs run over the two rows: (mo[k], mo[C + k]).
+    const float2 c0 = make_float2(m[0], m[3]), c1 = make_float2(m[1], m[4]),
+                 c2 = make_float2(m[2], m[5]);
+    const float2 x = make_float2(p[0], p[1]), l = make_float2(lam[0], lam[1]);
+    const float2 v = __ffma2_rn(c0, bc(x.x), __ffma2_rn(c1, bc(x.y), c2));
+    const float2 q = __ffma2_rn(bc(h_half), v, x);
+    // at = A^T lam (linear part): at_k = m[C+k] lam1 + m[k] lam0.
+    const float2 at = make_float2(__fmaf_rn(m[3], l.y, __fmul_rn(m[0], l.x)),
+                                  __fmaf_rn(m[4], l.y, __fmul_rn(m[1], l.x)));
+    const float2 wq = __fmul2_rn(bc(h), l), wp = __fmul2_rn(bc(hh), at);
+    float2 m0 = make_float2(mo[0], mo[C]), m1 = make_float2(mo[1], mo[C + 1]),
+           m2 = make_float2(mo[2], mo[C + 2]);
+    m0 = __ffma2_rn(wq, bc(q.x), m0);
+    m1 = __ffma2_rn(wq, bc(q.y), m1);
+    m2 = __fadd2_rn(m2, wq);
+    m0 = __ffma2_rn(wp, bc(x.x), m0);
+    m1 = __ffma2_rn(wp, bc(x.y), m1);
+    m2 = __fadd2_rn(m2, wp);
+    mo[0] = m0.x; mo[1] = m1.x; mo[2] = m2.x;
+    mo[C] = m0.y; mo[C + 1] = m1.y; mo[C + 2] = m2.y;
+    const float2 lm = __ffma2_rn(bc(h_half), at, l);
+    const float2 sv = make_float2(__fmaf_rn(m[3], lm.y, __fmul_rn(m[0], lm.x)),
+                                  __fmaf_rn(m[4], lm.y, __fmul_rn(m[1], lm.x)));
+    const float2 ln = __ffma2_rn(bc(h), sv, l);
+    lam[0] = ln.x;
+    lam[1] = ln.y;
+    return;
+  }
   float v[ND], q[ND], at[ND];
   affine<ND>(m, p, v);
 #pragma unroll
@@ -319,50 +420,24 @@ __device__ __forceinline__ void adjoint_step(const float (&m)[Dim<ND>::kPpc], co
   }
 }
 
-// Flush one cell's partial moments into a shared-memory table.
+// Flush one cell's partial moments into the global moment table with vector
+// reductions (red.global.add.v4/v2.f32, resolved in L2; fire and forget):
+// P/4 or P/2 instructions per flush.  A shared-memory table would cost far
+// more here: fp32 atomics on shared memory are compare-and-swap loops, and the
+// lanes of a warp (processing points sorted by cell) usually hit the same
+// cell, so those loops retry once per lane.  g_mom must be 16-byte aligned
+// when P % 4 == 0 (3D rows of 12 floats), else 8-byte aligned.
 template <int P>
-__device__ __forceinline__ void flush_smem(float *__restrict__ s_mom, int c, float (&mo)[P]) {
-  float *dst = s_mom + c * P;
+__device__ __forceinline__ void flush_moments(float *__restrict__ g_mom, int c, float (&mo)[P]) {
+  if constexpr (P % 4 == 0) {
+    float4 *dst = reinterpret_cast<float4 *>(g_mom + (int64_t)c * P);
 #pragma unroll
-  for (int k = 0; k < P; ++k) {
-    atomicAdd(dst + k, mo[k]);
-    mo[k] = 0.0f;
-  }
-}
-
-// Flush one cell's partial moments straight to global memory.  Lanes of the
-// warp that flush the same cell are summed first, so each cell costs one
-// atomic per moment per warp.
-template <int P>
-__device__ __forceinline__ void flush_global(float *__restrict__ g_mom, int c, float (&mo)[P]) {
-  const unsigned active = __activemask();
-  const unsigned same = __match_any_sync(active, c);
-  const int lane = threadIdx.x & 31;
-  const int leader = __ffs(same) - 1;
-  if (same != (1u << lane)) {
-    // Sum the group's values into the leader, one peer at a time.
-    unsigned rest = same & ~(1u << leader);
-    float acc[P];
-#pragma unroll
-    for (int k = 0; k < P; ++k) acc[k] = mo[k];
-    while (rest) {
-      const int src = __ffs(rest) - 1;
-      rest &= rest - 1;
-#pragma unroll
-      for (int k = 0; k < P; ++k) {
-        const float v = __shfl_sync(same, mo[k], src);
-        acc[k] += v;
-      }
-    }
-    if (lane == leader) {
-      float *dst = g_mom + (int64_t)c * P;
-#pragma unroll
-      for (int k = 0; k < P; ++k) atomicAdd(dst + k, acc[k]);
-    }
+    for (int k = 0; k < P / 4; ++k)
+      atomicAdd(dst + k, make_float4(mo[4 * k], mo[4 * k + 1], mo[4 * k + 2], mo[4 * k + 3]));
   } else {
-    float *dst = g_mom + (int64_t)c * P;
+    float2 *dst = reinterpret_cast<float2 *>(g_mom + (int64_t)c * P);
 #pragma unroll
-    for (int k = 0; k < P; ++k) atomicAdd(dst + k, mo[k]);
+    for (int k = 0; k < P / 2; ++k) atomicAdd(dst + k, make_float2(mo[2 * k], mo[2 * k + 1]));
   }
 #pragma unroll
   for (int k = 0; k < P; ++k) mo[k] = 0.0f;

@@ -9,10 +9,10 @@
 //     points;
 //   * cell tables live in shared memory when they fit (padded to 128-bit
 //     rows), else they are read through the read-only cache with vector loads;
-//   * the adjoint keeps each replayed 8-step segment in registers (fully
-//     unrolled), checkpoints every 8 steps, and flushes per-cell moments into
-//     a block-wide shared-memory moment table that is written to global memory
-//     once per block -- instead of per-crossing global atomics.
+//   * the adjoint checkpoints every kSegSteps steps and records each step's
+//     cell, replays one segment at a time into registers, and flushes a
+//     thread's per-cell moments with vector L2 reductions only when its cell
+//     changes.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,8 +32,8 @@ template <int ND> struct BwdShape {
   static constexpr int kThreads = ND == 3 ? 256 : 512;
   static constexpr int kMinBlocks = 2;
 };
-// Shared-memory budget per block (cell table, plus the moment table in the
-// backward): two 512-thread blocks per SM give 32 resident warps.
+// Shared-memory budget per block for the cell table (two resident blocks per
+// SM at the largest table).
 constexpr size_t kFwdSmemBudget = 100 * 1024;
 constexpr size_t kBwdSmemBudget = 110 * 1024;
 
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
   const float *tg = a.trels + (int64_t)b * a.nC * P;
   const float *ag = a.As + (int64_t)b * a.nC * P;
   if constexpr (SMEM) {
-    stage_table(s_tab, tg, a.nC * P);
+    stage_table<ND>(s_tab, tg, a.nC);
     __syncthreads();
   }
   const float *tab = SMEM ? s_tab : tg;
@@ -190,25 +190,22 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
 // ---------------------------------------------------------------------------
 
 // CellT: type of the per-step cell record (uint16_t when nC <= 65535).
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, typename CellT>
+template <int ND, bool ADAPT, bool A_SMEM, typename CellT>
 __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
     k_backward(IntegrateArgs a) {
   constexpr int P = Dim<ND>::kPpc;
   constexpr int S = kSegSteps;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
-  float *s_mom = s_tab + (A_SMEM ? a.nC * P : 0);
   const int b = blockIdx.y;
   const int nC = a.nC;
   const float *ag = a.As + (int64_t)b * nC * P;
-  float *gm = a.moments + (int64_t)b * nC * P;
-  if constexpr (A_SMEM) stage_table(s_tab, ag, nC * P);
-  if constexpr (M_SMEM) {
-    for (int i = threadIdx.x; i < nC * P; i += blockDim.x) s_mom[i] = 0.0f;
+  float *mom = a.moments + (int64_t)b * nC * P;
+  if constexpr (A_SMEM) {
+    stage_table<ND>(s_tab, ag, nC);
+    __syncthreads();
   }
-  if constexpr (A_SMEM || M_SMEM) __syncthreads();
   const float *tab = A_SMEM ? s_tab : ag;
-  float *mom = M_SMEM ? s_mom : gm;
 
   const Tess t = a.tess;
   const int T = a.T;
@@ -295,10 +292,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
         if (kTail && s >= rem) continue;
         const int c = cs[s];
         if (c != prev) {
-          if (prev >= 0) {
-            if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
-            else flush_global<P>(mom, prev, mo);
-          }
+          if (prev >= 0) flush_moments<P>(mom, prev, mo);
           prev = c;
         }
         float m[P];
@@ -308,21 +302,10 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
     };
     if (rem) phase2(nfull, std::true_type{});
     for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
-    if (prev >= 0) {
-      if constexpr (M_SMEM) flush_smem<P>(mom, prev, mo);
-      else flush_global<P>(mom, prev, mo);
-    }
+    if (prev >= 0) flush_moments<P>(mom, prev, mo);
     if (gp) {
 #pragma unroll
       for (int k = 0; k < ND; ++k) gp[k * nP + i] = lam[k];
-    }
-  }
-
-  if constexpr (M_SMEM) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < nC * P; i += blockDim.x) {
-      const float v = s_mom[i];
-      if (v != 0.0f) atomicAdd(gm + i, v);
     }
   }
 }
@@ -350,18 +333,32 @@ __global__ void k_cell_index(Tess t, const float *__restrict__ pts, int64_t n,
 // flushes).  counts is [n_sets, nC] int32 scratch.
 // ---------------------------------------------------------------------------
 
-template <int ND>
+// Histogram of initial cells.  With SMEM, each block counts its contiguous
+// chunk of points in shared memory and adds its non-zero bins to the global
+// counts (one atomic per block and non-empty cell instead of one per point).
+template <int ND, bool SMEM>
 __global__ void k_cell_histogram(Tess t, const float *__restrict__ pts, int64_t nP, int nC,
                                  int32_t *__restrict__ counts) {
+  extern __shared__ int32_t s_cnt[];
   const int set = blockIdx.y;
   const float *p0 = pts + (int64_t)set * ND * nP;
   int32_t *cnt = counts + (int64_t)set * nC;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t chunk = (nP + gridDim.x - 1) / gridDim.x;
+  const int64_t lo = blockIdx.x * chunk, hi = min(nP, lo + chunk);
+  if constexpr (SMEM) {
+    for (int c = threadIdx.x; c < nC; c += blockDim.x) s_cnt[c] = 0;
+    __syncthreads();
+  }
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
     float p[ND];
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(p0 + k * nP + i);
-    atomicAdd(cnt + lookup<ND>(t, p), 1);
+    atomicAdd((SMEM ? s_cnt : cnt) + lookup<ND>(t, p), 1);
+  }
+  if constexpr (SMEM) {
+    __syncthreads();
+    for (int c = threadIdx.x; c < nC; c += blockDim.x)
+      if (s_cnt[c]) atomicAdd(cnt + c, s_cnt[c]);
   }
 }
 
@@ -389,19 +386,40 @@ __global__ void __launch_bounds__(1024) k_exclusive_scan(int32_t *__restrict__ c
   }
 }
 
-template <int ND>
+// Scatter the points to their sorted positions.  With SMEM, each block counts
+// its chunk per cell in shared memory, reserves one range per non-empty cell
+// with a single global atomic, then places its points inside those ranges.
+template <int ND, bool SMEM>
 __global__ void k_cell_scatter(Tess t, const float *__restrict__ pts, int64_t nP, int nC,
                                int32_t *__restrict__ offsets, int32_t *__restrict__ order) {
+  extern __shared__ int32_t s_cnt[];
   const int set = blockIdx.y;
   const float *p0 = pts + (int64_t)set * ND * nP;
   int32_t *off = offsets + (int64_t)set * nC;
   int32_t *ord = order + (int64_t)set * nP;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nP;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t chunk = (nP + gridDim.x - 1) / gridDim.x;
+  const int64_t lo = blockIdx.x * chunk, hi = min(nP, lo + chunk);
+  if constexpr (SMEM) {
+    for (int c = threadIdx.x; c < nC; c += blockDim.x) s_cnt[c] = 0;
+    __syncthreads();
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      float p[ND];
+#pragma unroll
+      for (int k = 0; k < ND; ++k) p[k] = __ldg(p0 + k * nP + i);
+      atomicAdd(s_cnt + lookup<ND>(t, p), 1);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < nC; c += blockDim.x) {
+      const int32_t n = s_cnt[c];
+      s_cnt[c] = n ? atomicAdd(off + c, n) : 0;  // this block's first slot in cell c
+    }
+    __syncthreads();
+  }
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
     float p[ND];
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(p0 + k * nP + i);
-    ord[atomicAdd(off + lookup<ND>(t, p), 1)] = (int32_t)i;
+    ord[atomicAdd((SMEM ? s_cnt : off) + lookup<ND>(t, p), 1)] = (int32_t)i;
   }
 }
 
@@ -473,13 +491,10 @@ cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
 template <int ND, bool ADAPT, typename CellT>
 cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
-  const size_t mom = tab;
   constexpr int kT = BwdShape<ND>::kThreads;
-  if (tab + mom <= kBwdSmemBudget)
-    return launch_wave(k_backward<ND, ADAPT, true, true, CellT>, kT, tab + mom, a, s);
-  if (mom <= kBwdSmemBudget)
-    return launch_wave(k_backward<ND, ADAPT, false, true, CellT>, kT, mom, a, s);
-  return launch_wave(k_backward<ND, ADAPT, false, false, CellT>, kT, 0, a, s);
+  if (tab <= kBwdSmemBudget)
+    return launch_wave(k_backward<ND, ADAPT, true, CellT>, kT, tab, a, s);
+  return launch_wave(k_backward<ND, ADAPT, false, CellT>, kT, 0, a, s);
 }
 
 template <int ND, bool ADAPT>
@@ -529,21 +544,53 @@ cudaError_t launch_order_points(int ndim, Tess t, const float *points, int64_t n
   if (nP == 0 || n_sets == 0) return cudaSuccess;
   cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)n_sets * nC * sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
-  int64_t bx = (nP + 255) / 256;
-  const int64_t cap = (int64_t)device_info().sm_count * 8;
-  if (bx > cap) bx = cap;
+  // Shared-memory counts when the cell table fits; then about 4 points per
+  // cell per block keeps the per-block flush small against the chunk's work.
+  const size_t smem = (size_t)nC * sizeof(int32_t);
+  const bool use_smem = smem <= 128 * 1024;
+  int64_t bx;
+  if (use_smem) {
+    // At least ~4 points per cell per block (so the per-block flush of nC bins
+    // stays small against the chunk's work), at least 4096 points per block,
+    // at most two blocks per SM.
+    bx = nP / (nP > 64 * (int64_t)nC ? 4096 : 4 * (int64_t)nC + 1024);
+    const int64_t cap = (int64_t)device_info().sm_count * 2 / n_sets;
+    bx = bx > cap ? cap : bx;
+  } else {
+    bx = (nP + 255) / 256;
+    const int64_t cap = (int64_t)device_info().sm_count * 8;
+    bx = bx > cap ? cap : bx;
+  }
+  if (bx < 1) bx = 1;
   const dim3 grid((unsigned)bx, (unsigned)n_sets);
-  switch (ndim) {
-    case 1: k_cell_histogram<1><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
-    case 2: k_cell_histogram<2><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
-    default: k_cell_histogram<3><<<grid, 256, 0, s>>>(t, points, nP, nC, counts); break;
+  const int thr = use_smem ? 512 : 256;
+  const size_t sm = use_smem ? smem : 0;
+#define CPAB_ORDER_LAUNCH(KERNEL, ...)                                                     \
+  do {                                                                                     \
+    if (use_smem) {                                                                        \
+      switch (ndim) {                                                                      \
+        case 1: KERNEL<1, true><<<grid, thr, sm, s>>>(__VA_ARGS__); break;                 \
+        case 2: KERNEL<2, true><<<grid, thr, sm, s>>>(__VA_ARGS__); break;                 \
+        default: KERNEL<3, true><<<grid, thr, sm, s>>>(__VA_ARGS__); break;                \
+      }                                                                                    \
+    } else {                                                                               \
+      switch (ndim) {                                                                      \
+        case 1: KERNEL<1, false><<<grid, thr, 0, s>>>(__VA_ARGS__); break;                 \
+        case 2: KERNEL<2, false><<<grid, thr, 0, s>>>(__VA_ARGS__); break;                 \
+        default: KERNEL<3, false><<<grid, thr, 0, s>>>(__VA_ARGS__); break;                \
+      }                                                                                    \
+    }                                                                                      \
+  } while (0)
+  if (use_smem && smem > 48 * 1024) {
+    for (auto k : {(const void *)k_cell_histogram<1, true>, (const void *)k_cell_histogram<2, true>,
+                   (const void *)k_cell_histogram<3, true>, (const void *)k_cell_scatter<1, true>,
+                   (const void *)k_cell_scatter<2, true>, (const void *)k_cell_scatter<3, true>})
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
   }
+  CPAB_ORDER_LAUNCH(k_cell_histogram, t, points, nP, nC, counts);
   k_exclusive_scan<<<n_sets, 1024, 0, s>>>(counts, nC);
-  switch (ndim) {
-    case 1: k_cell_scatter<1><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
-    case 2: k_cell_scatter<2><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
-    default: k_cell_scatter<3><<<grid, 256, 0, s>>>(t, points, nP, nC, counts, order); break;
-  }
+  CPAB_ORDER_LAUNCH(k_cell_scatter, t, points, nP, nC, counts, order);
+#undef CPAB_ORDER_LAUNCH
   return cudaGetLastError();
 }
 

@@ -118,7 +118,9 @@ int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP,
  * (nstepsolver steps, Heun on crossings when adaptive = 1), walks it backwards
  * from lambda(1) = grad_out and accumulates the per-cell moments
  *   M_c += h lam p_mid^T + (h^2/2) (A_c^T lam) p^T    (as [n_theta, nC, ppc]).
- * moments is overwritten (zeroed here first).  When grad_points != NULL it
+ * moments (16-byte aligned) is overwritten (zeroed here first); its sums are
+ * fp32 reductions in L2, so their last bits vary from run to run.  When
+ * grad_points != NULL it
  * receives lambda(0) as [n_theta, ndim, nP] (the reference's grad_points
  * before its optional batch sum).
  * Replaces cpab/pytorch/transformer_cuda.cpp:92-116 and :122-153.

@@ -531,20 +531,36 @@ void oracle_midpoint_forward(int nd, const int32_t *nc, const float *pts, int64_
   }
 }
 
-/* out[t, r] = sum over row r of a CSR matrix of vals * x[t, col], accumulated
- * in float32 with fmaf in stored (column) order: an fp32 sparse product as the
- * reference's torch.sparse.mm computes A = B theta^T and dtheta = B^T m
- * (cpab/pytorch/transformer.py:84, :166). */
+/* out[t, r] = sum over row r of a CSR matrix of vals * x[t, col] in float32,
+ * in the order the GPU kernels use (the reference computes these products with
+ * torch.sparse.mm, cpab/pytorch/transformer.py:84 and :166, whose fp32 order
+ * is the library's): 32 lane partials, lane l accumulating nonzeros
+ * l, l+32, ... of the row with fmaf, then an xor butterfly over the lanes with
+ * offsets 16, 8, 4, 2, 1 (lane 0's value is returned). */
+static float warp_order_dot(const int32_t *colidx, const float *vals, int32_t k0, int32_t k1,
+                            const float *x) {
+  float lane[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int32_t k = k0 + l; k < k1; k += 32) s = fmaf(vals[k], x[colidx[k]], s);
+    lane[l] = s;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    float next[32];
+    for (int l = 0; l < 32; ++l) next[l] = lane[l] + lane[l ^ off];
+    memcpy(lane, next, sizeof(lane));
+  }
+  return lane[0];
+}
+
 void oracle_csr_matmul(int64_t rows, const int32_t *rowptr, const int32_t *colidx,
                        const float *vals, int n_rhs, const float *x, int64_t x_stride,
                        float *out, int64_t out_stride) {
 #pragma omp parallel for collapse(2) schedule(static)
   for (int t = 0; t < n_rhs; ++t) {
     for (int64_t r = 0; r < rows; ++r) {
-      const float *xt = x + (int64_t)t * x_stride;
-      float s = 0.0f;
-      for (int32_t k = rowptr[r]; k < rowptr[r + 1]; ++k) s = fmaf(vals[k], xt[colidx[k]], s);
-      out[(int64_t)t * out_stride + r] = s;
+      out[(int64_t)t * out_stride + r] =
+          warp_order_dot(colidx, vals, rowptr[r], rowptr[r + 1], x + (int64_t)t * x_stride);
     }
   }
 }

@@ -5,9 +5,9 @@ CPU-baseline legs of bench.py, as the checker -- never by the product.
 
   * integration / adjoint / expm / cell lookup: liboracle.so, the C
     restatement in cpab_oracle.c (cpab/core/cpab_ops_{1,2,3}d.cu);
-  * A = B theta and dtheta = B^T m: fp32 CSR products (fma in stored order),
-    as torch.sparse.mm computes them in cpab/pytorch/transformer.py:84-88,
-    :165-166;
+  * A = B theta and dtheta = B^T m: fp32 CSR products summed in the GPU
+    kernels' fixed order (lane partials + xor butterfly), as torch.sparse.mm
+    computes them in cpab/pytorch/transformer.py:84-88, :165-166;
   * resampling: numpy float32 restatement of cpab/pytorch/interpolation.py:8-160
     (forward, op for op) and of the gradient its autograd graph produces.
 
@@ -108,7 +108,9 @@ def _csr32(M):
 
 
 def csr_matmul(M, X):
-    """(M @ X^T)^T for a sparse M [rows, cols] and X [n, cols], fp32 fma in CSR order."""
+    """(M @ X^T)^T for a sparse M [rows, cols] and X [n, cols] in fp32, summed
+    in the GPU kernels' order (32 strided lane partials with fma, then an xor
+    butterfly over the lanes)."""
     X = _f32(X)
     rp, ci, v = _csr32(M)
     rows = M.shape[0]
