@@ -227,13 +227,31 @@ __global__ void k_expm(const float *__restrict__ As, int64_t n, float dT, float 
   for (int k = 0; k < P; ++k) trels[i * P + k] = r[k];
 }
 
-// One warp per cell.  For each transformation t the warp forms the cell's kPpc
-// entries A[t, c, r] = sum_k B[r, k] theta[t, k]: the row's nonzeros are split
-// over the lanes and summed with a butterfly (the column indices of a row are
-// clustered, so the lanes' theta loads share sectors).  Lane t keeps
-// transformation t's entries and then computes that cell's exponential, so
-// the expm work runs 32 transformations wide.  Rows of a zero-boundary basis
-// have <= 4 nonzeros; general bases have dozens.
+// Dot product of CSR row [k0, k1) with x split over the 32 lanes of a warp:
+// lane l sums products k0 + l, k0 + l + 32, ... with an fmaf chain, an xor
+// butterfly adds the lane partials; every lane returns the sum.  (The CPU
+// oracle restates this order.)
+__device__ __forceinline__ float warp_dot(const int32_t *__restrict__ colidx,
+                                          const float *__restrict__ vals, int k0, int k1,
+                                          const float *__restrict__ x) {
+  float sum = 0.0f;
+  for (int k = k0 + (threadIdx.x & 31); k < k1; k += 32)
+    sum = fmaf(__ldg(vals + k), __ldg(x + __ldg(colidx + k)), sum);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  return sum;
+}
+
+// A = B theta (and Trels = expm(A dT) when trels != NULL), in one of two
+// mappings chosen on the device from B's nonzeros (rowptr[nC * P], one
+// broadcast load, so the host needs no copy and the call stays asynchronous):
+//   * sparse B (at most 4 nonzeros per row on average; zero-boundary bases
+//     have <= 4 in every row): one thread per (transformation, cell), each row
+//     summed with a sequential fmaf chain;
+//   * otherwise one warp per cell: each row's nonzeros split over the lanes
+//     (warp_dot), lane j keeping transformation t0 + j's entries, then each
+//     lane computes the exponential, 32 transformations wide.
+// The grid covers nC warps; the sparse mapping strides over nC * n_theta.
 template <int ND>
 __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_theta,
                                                  const int32_t *__restrict__ rowptr,
@@ -243,7 +261,34 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
                                                  float *__restrict__ As,
                                                  float *__restrict__ trels) {
   constexpr int P = Dim<ND>::kPpc;
-  const int64_t c = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t gtid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const bool sparse = __ldg(rowptr + nC * P) <= 4 * nC * P;
+  if (sparse) {
+    const int64_t n = nC * n_theta;
+    for (int64_t i = gtid; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = i / nC;
+      const int64_t c = i - t * nC;
+      const float *th = theta + t * d;
+      float a[P];
+#pragma unroll
+      for (int r = 0; r < P; ++r) {
+        const int k0 = __ldg(rowptr + c * P + r), k1 = __ldg(rowptr + c * P + r + 1);
+        float sum = 0.0f;
+        for (int k = k0; k < k1; ++k) sum = fmaf(__ldg(vals + k), __ldg(th + __ldg(colidx + k)), sum);
+        a[r] = sum;
+      }
+#pragma unroll
+      for (int r = 0; r < P; ++r) As[i * P + r] = a[r];
+      if (trels != nullptr) {
+        float e[P];
+        expm_cell<ND>(a, dT, e);
+#pragma unroll
+        for (int r = 0; r < P; ++r) trels[i * P + r] = e[r];
+      }
+    }
+    return;
+  }
+  const int64_t c = gtid >> 5;
   const int lane = threadIdx.x & 31;
   if (c >= nC) return;  // whole warps exit together
   int k0[P], k1[P];
@@ -261,11 +306,7 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
       const float *th = theta + (int64_t)(t0 + j) * d;
 #pragma unroll
       for (int r = 0; r < P; ++r) {
-        float sum = 0.0f;
-        for (int k = k0[r] + lane; k < k1[r]; k += 32)
-          sum = fmaf(__ldg(vals + k), __ldg(th + __ldg(colidx + k)), sum);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        const float sum = warp_dot(colidx, vals, k0[r], k1[r], th);
         if (lane == j) mine[r] = sum;
       }
     }
@@ -284,9 +325,9 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
 }
 
 // dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].  One warp
-// per basis column j: the lanes split the row's nonzeros (clustered column
-// indices, so the moment gathers share sectors) and a butterfly sums each
-// transformation's dot product.
+// per basis column j (warp_dot; clustered column indices let the moment
+// gathers share sectors).  Columns have 16 to 80 nonzeros for zero-boundary
+// bases and up to ~1,700 for general ones.
 __global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_theta,
                                                  const int32_t *__restrict__ rowptr,
                                                  const int32_t *__restrict__ colidx,
@@ -294,16 +335,11 @@ __global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_the
                                                  const float *__restrict__ moments,
                                                  float *__restrict__ dtheta) {
   const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
   if (j >= d) return;
   const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
   for (int t = 0; t < n_theta; ++t) {
-    const float *m = moments + (int64_t)t * D;
-    float sum = 0.0f;
-    for (int k = k0 + lane; k < k1; k += 32) sum = fmaf(__ldg(vals + k), __ldg(m + __ldg(colidx + k)), sum);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (lane == 0) dtheta[(int64_t)t * d + j] = sum;
+    const float sum = warp_dot(colidx, vals, k0, k1, moments + (int64_t)t * D);
+    if ((threadIdx.x & 31) == 0) dtheta[(int64_t)t * d + j] = sum;
   }
 }
 

@@ -193,8 +193,10 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float 
 // 2D table staged in shared memory is stored by column pairs instead --
 // (m00, m10), (m01, m11), (m02, m12) -- so that both rows of a step are
 // evaluated with paired fp32 instructions; it is still 24 bytes a cell, three
-// 64-bit words.  A 3D row is 48 bytes, three 128-bit words.  Packed rows
-// spread neighbouring cells over distinct shared-memory banks.
+// 64-bit words.  A 3D row is 48 bytes, three 128-bit words, in the reference
+// layout everywhere (3D tables rarely fit shared memory, and the 3D adjoint
+// pairs neighbours within a row).  Packed rows spread neighbouring cells over
+// distinct shared-memory banks.
 // ---------------------------------------------------------------------------
 
 template <int ND, bool SMEM>
@@ -300,6 +302,16 @@ __device__ __forceinline__ void midpoint_step(const float (&m)[Dim<ND>::kPpc], f
     p[0] = y.x;
     p[1] = y.y;
     return;
+  } else if constexpr (ND == 3) {
+    float v[3], q[3], w[3];
+    affine<3>(m, p, v);
+    const float2 x = make_float2(p[0], p[1]);
+    const float2 q01 = __ffma2_rn(bc(h_half), make_float2(v[0], v[1]), x);
+    q[0] = q01.x; q[1] = q01.y; q[2] = __fmaf_rn(h_half, v[2], p[2]);
+    affine<3>(m, q, w);
+    const float2 y = __ffma2_rn(bc(h), make_float2(w[0], w[1]), x);
+    p[0] = y.x; p[1] = y.y; p[2] = __fmaf_rn(h, w[2], p[2]);
+    return;
   }
   float v[ND], q[ND], w[ND];
   affine<ND>(m, p, v);
@@ -380,6 +392,42 @@ __device__ __forceinline__ void adjoint_step(const float (&m)[Dim<ND>::kPpc], co
     lam[0] = ln.x;
     lam[1] = ln.y;
     return;
+  } else if constexpr (ND == 3) {
+    // Row layout: the A^T products pair entries k = 0, 1 of each row, the
+    // moment updates pair (mo[r][0], mo[r][1]) and (mo[r][2], mo[r][3]); the
+    // constant column's update mo += w is written fma(w, 1, mo), which rounds
+    // identically.
+    float v[3];
+    affine<3>(m, p, v);
+    const float2 p01 = make_float2(p[0], p[1]), l01 = make_float2(lam[0], lam[1]);
+    const float2 q01 = __ffma2_rn(bc(h_half), make_float2(v[0], v[1]), p01);
+    const float q2 = __fmaf_rn(h_half, v[2], p[2]);
+    const float2 r0 = make_float2(m[0], m[1]), r1 = make_float2(m[C], m[C + 1]),
+                 r2 = make_float2(m[2 * C], m[2 * C + 1]);
+    const float2 at01 = __ffma2_rn(r2, bc(lam[2]), __ffma2_rn(r1, bc(lam[1]), __fmul2_rn(r0, bc(lam[0]))));
+    const float at2 = __fmaf_rn(m[2 * C + 2], lam[2], __fmaf_rn(m[C + 2], lam[1], __fmul_rn(m[2], lam[0])));
+    const float2 wq01 = __fmul2_rn(bc(h), l01), wp01 = __fmul2_rn(bc(hh), at01);
+    const float wq[3] = {wq01.x, wq01.y, __fmul_rn(h, lam[2])};
+    const float wp[3] = {wp01.x, wp01.y, __fmul_rn(hh, at2)};
+    const float2 q2one = make_float2(q2, 1.0f), p2one = make_float2(p[2], 1.0f);
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      float2 a = make_float2(mo[r * C], mo[r * C + 1]), b = make_float2(mo[r * C + 2], mo[r * C + 3]);
+      a = __ffma2_rn(bc(wq[r]), q01, a);
+      b = __ffma2_rn(bc(wq[r]), q2one, b);
+      a = __ffma2_rn(bc(wp[r]), p01, a);
+      b = __ffma2_rn(bc(wp[r]), p2one, b);
+      mo[r * C] = a.x; mo[r * C + 1] = a.y; mo[r * C + 2] = b.x; mo[r * C + 3] = b.y;
+    }
+    const float2 lm01 = __ffma2_rn(bc(h_half), at01, l01);
+    const float lm2 = __fmaf_rn(h_half, at2, lam[2]);
+    const float2 s01 = __ffma2_rn(r2, bc(lm2), __ffma2_rn(r1, bc(lm01.y), __fmul2_rn(r0, bc(lm01.x))));
+    const float s2 = __fmaf_rn(m[2 * C + 2], lm2, __fmaf_rn(m[C + 2], lm01.y, __fmul_rn(m[2], lm01.x)));
+    const float2 ln = __ffma2_rn(bc(h), s01, l01);
+    lam[2] = __fmaf_rn(h, s2, lam[2]);
+    lam[0] = ln.x;
+    lam[1] = ln.y;
+    return;
   }
   float v[ND], q[ND], at[ND];
   affine<ND>(m, p, v);
@@ -417,6 +465,18 @@ __device__ __forceinline__ void adjoint_step(const float (&m)[Dim<ND>::kPpc], co
 #pragma unroll
     for (int r = 1; r < ND; ++r) s = s + m[r * C + k] * lm[r];
     lam[k] += h * s;
+  }
+}
+
+// Flush one cell's partial moments into a shared-memory table (fp32 atomics on
+// shared memory: a compare-and-swap loop each).
+template <int P>
+__device__ __forceinline__ void flush_smem(float *__restrict__ s_mom, int c, float (&mo)[P]) {
+  float *dst = s_mom + c * P;
+#pragma unroll
+  for (int k = 0; k < P; ++k) {
+    atomicAdd(dst + k, mo[k]);
+    mo[k] = 0.0f;
   }
 }
 

@@ -46,7 +46,7 @@ def lib():
         L.oracle_midpoint_forward.argtypes = [_c_int, _p, _p, _c_i64, _c_int, _p, _c_int, _c_int,
                                               _c_int, _p]
         L.oracle_midpoint_forward.restype = None
-        L.oracle_csr_matmul.argtypes = [_c_i64, _p, _p, _p, _c_int, _p, _c_i64, _p, _c_i64]
+        L.oracle_csr_matmul.argtypes = [_c_i64, _p, _p, _p, _c_int, _p, _c_i64, _p, _c_i64, _c_int]
         L.oracle_csr_matmul.restype = None
         L.oracle_num_threads.restype = _c_int
         L.oracle_set_num_threads.argtypes = [_c_int]
@@ -107,16 +107,16 @@ def _csr32(M):
             np.ascontiguousarray(M.data, np.float32))
 
 
-def csr_matmul(M, X):
+def csr_matmul(M, X, lanes=32):
     """(M @ X^T)^T for a sparse M [rows, cols] and X [n, cols] in fp32, summed
-    in the GPU kernels' order (32 strided lane partials with fma, then an xor
-    butterfly over the lanes)."""
+    in the GPU kernels' order: lanes = 1, one fma chain per row; lanes = 32,
+    32 strided lane partials with fma, then an xor butterfly over the lanes."""
     X = _f32(X)
     rp, ci, v = _csr32(M)
     rows = M.shape[0]
     out = np.empty((X.shape[0], rows), dtype=np.float32)
     lib().oracle_csr_matmul(rows, _ptr(rp), _ptr(ci), _ptr(v), X.shape[0], _ptr(X), X.shape[1],
-                            _ptr(out), rows)
+                            _ptr(out), rows, lanes)
     return out
 
 
@@ -124,7 +124,11 @@ def build_A(basis, theta, ndim):
     """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T (fp32)."""
     th = _f32(theta)
     nC = basis.shape[0] // (ndim * (ndim + 1))
-    return csr_matmul(basis, th).reshape(th.shape[0], nC, ndim, ndim + 1)
+    # k_build_A's mapping: a chain per entry when B has <= 4 nonzeros per row
+    # on average, else rows split over a warp.
+    nnz = len(_csr32(basis)[1])
+    lanes = 1 if nnz <= 4 * basis.shape[0] else 32
+    return csr_matmul(basis, th, lanes).reshape(th.shape[0], nC, ndim, ndim + 1)
 
 
 def project(basis, moments):
