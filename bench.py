@@ -33,6 +33,7 @@ for _p in (os.path.join(ROOT, "fg-cpab_b200"), ROOT):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
 
 TESS = [20, 20]
 BATCH = 16
@@ -265,7 +266,8 @@ def make_workload(name, rank, world, dev):
             t = x["theta"].requires_grad_(True)
             pts = x["points"]
             out = C.transform_grid(pts, t) if group is None else transform_grid_sharded(C, pts, t, group)
-            loss = ((out - pts) ** 2).sum() if nd == 1 else ((out - pts) ** 2).mean()
+            ref = pts.expand_as(out)
+            loss = F.mse_loss(out, ref, reduction="sum" if nd == 1 else "mean")
             loss.backward()
             return loss, t.grad
         return w, C, host, step, B * nP
@@ -295,7 +297,7 @@ def make_workload(name, rank, world, dev):
         def step(x):
             t = x["theta"].requires_grad_(True)
             out = C.transform_data(x["data"], t, outsize)
-            loss = ((out - x["target"]) ** 2).mean()
+            loss = F.mse_loss(out, x["target"])
             loss.backward()
             return loss, t.grad
         return w, C, host, step, B * int(np.prod(outsize))
@@ -316,7 +318,7 @@ def make_workload(name, rank, world, dev):
             if group is not None:
                 allreduce_theta_grad(t, group)
             out = C.transform_grid_chain(x["points"], t, scale_by_dt=True)
-            loss = ((out - x["points"]) ** 2).sum()
+            loss = F.mse_loss(out, x["points"].expand_as(out), reduction="sum")
             loss.backward()
             return loss, t.grad
         return w, C, host, step, grid.shape[1] * K

@@ -99,6 +99,30 @@ def _nc(params):
 ORDER_MIN_POINTS = 4096
 
 
+def _order(params, points, batched):
+    """Processing order of ``points`` (sorted by initial cell), or None.
+
+    The order depends on the points only, and callers usually transform the
+    same points (a fixed meshgrid) under changing theta, so the last order is
+    kept per device, keyed on the tensor's storage pointer, version counter
+    and shape.  A stale hit (a new tensor at a reused address) is harmless:
+    results never depend on the processing order, which is always a
+    permutation of the right size.
+    """
+    nP = points.shape[-1]
+    if nP < ORDER_MIN_POINTS:
+        return None
+    cache = params.__dict__.setdefault("_order_cache", {})
+    key = (points.data_ptr(), points._version, tuple(points.shape), bool(batched),
+           tuple(_nc(params)))
+    hit = cache.get(points.device)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    order = _native.order_points(_nc(params), points, batched)
+    cache[points.device] = (key, order)
+    return order
+
+
 class _CPABFunction(torch.autograd.Function):
     """A = B theta -> integrate; backward: fused adjoint moments -> B^T projection."""
 
@@ -113,8 +137,7 @@ class _CPABFunction(torch.autograd.Function):
         adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
         dT = None if nd == 1 else 1.0 / T
         As, trels = _native.build_A(nd, int(params.nC), basis, theta_c, dT)
-        order = (_native.order_points(_nc(params), points_c, batched)
-                 if points_c.shape[-1] >= ORDER_MIN_POINTS else None)
+        order = _order(params, points_c, batched)
         out = _native.forward(nd, _nc(params), points_c, batched, trels, As, T, adaptive, order)
         ctx.params = params
         ctx.batched = batched

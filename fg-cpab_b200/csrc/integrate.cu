@@ -196,7 +196,11 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
 // reductions (measured: 1D backward 195 us with L2 reductions, 160 us with the
 // shared table); with many cells the shared table's compare-and-swap loops
 // cost more, so 2D/3D reduce in L2.
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, typename CellT>
+// CL_SMEM: the per-step cell record lives in shared memory, [T][blockDim]
+// (a warp's 32 entries of one step are 64 contiguous bytes), instead of in
+// each thread's local memory, whose ~200 bytes per thread across ~150k
+// resident threads overflow L1 into L2 and DRAM.
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT>
 __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
     k_backward(IntegrateArgs a) {
   constexpr int P = Dim<ND>::kPpc;
@@ -204,6 +208,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
   float *s_mom = s_tab + (A_SMEM ? a.nC * P : 0);
+  CellT *s_cl = reinterpret_cast<CellT *>(s_mom + (M_SMEM ? a.nC * P : 0)) + threadIdx.x;
   const int b = blockIdx.y;
   const int nC = a.nC;
   const float *ag = a.As + (int64_t)b * nC * P;
@@ -246,7 +251,11 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
     // with compile-time trip counts; only the tail segment (T % S steps) is
     // guarded.
     float ck[kMaxSegs][ND];
-    CellT cl[ADAPT ? 1 : kMaxSteps];
+    CellT cl_local[(ADAPT || CL_SMEM) ? 1 : kMaxSteps];
+    auto cl = [&](int step) -> CellT & {
+      if constexpr (CL_SMEM) return s_cl[step * blockDim.x];
+      else return cl_local[step];
+    };
     auto phase1 = [&](int seg, auto tail) {
       constexpr bool kTail = decltype(tail)::value;
 #pragma unroll
@@ -258,7 +267,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
           replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
         } else {
           const int c = lookup<ND>(t, p);
-          cl[seg * S + s] = (CellT)c;
+          cl(seg * S + s) = (CellT)c;
           float m[P];
           load_cell<ND, A_SMEM>(tab, c, m);
           midpoint_step<ND>(m, p, h, h_half);
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
         if constexpr (ADAPT) {
           cs[s] = replay_step<ND, true, A_SMEM>(t, tab, p, h, h_half);
         } else {
-          cs[s] = (int)cl[seg * S + s];
+          cs[s] = (int)cl(seg * S + s);
           // The segment's end point is not needed.
           if (kTail ? s + 1 < rem : s + 1 < S) {
             float m[P];
@@ -508,17 +517,31 @@ cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
               : launch_wave(k_forward<ND, false, false>, kFwdThreads, 0, a, s);
 }
 
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, typename CellT>
+cudaError_t backward_launch(const IntegrateArgs &a, size_t smem, size_t cl, cudaStream_t s) {
+  constexpr int kT = BwdShape<ND>::kThreads;
+  if constexpr (!ADAPT && sizeof(CellT) == 2) {
+    if (cl > 0)
+      return launch_wave(k_backward<ND, ADAPT, A_SMEM, M_SMEM, true, CellT>, kT, smem + cl, a, s);
+  }
+  return launch_wave(k_backward<ND, ADAPT, A_SMEM, M_SMEM, false, CellT>, kT, smem, a, s);
+}
+
 template <int ND, bool ADAPT, typename CellT>
 cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
   constexpr int kT = BwdShape<ND>::kThreads;
+  // Shared memory, in order of preference: the cell table, the 1D moment
+  // table, the 16-bit cell record (when all of it fits the budget).
+  const size_t cl_bytes = (ADAPT || sizeof(CellT) != 2) ? 0 : (size_t)kT * a.T * sizeof(CellT);
+  auto cl_fits = [&](size_t used) { return used + cl_bytes <= kBwdSmemBudget ? cl_bytes : 0; };
   if constexpr (ND == 1) {
     if (2 * tab <= kBwdSmemBudget)
-      return launch_wave(k_backward<ND, ADAPT, true, true, CellT>, kT, 2 * tab, a, s);
+      return backward_launch<ND, ADAPT, true, true, CellT>(a, 2 * tab, cl_fits(2 * tab), s);
   }
   if (tab <= kBwdSmemBudget)
-    return launch_wave(k_backward<ND, ADAPT, true, false, CellT>, kT, tab, a, s);
-  return launch_wave(k_backward<ND, ADAPT, false, false, CellT>, kT, 0, a, s);
+    return backward_launch<ND, ADAPT, true, false, CellT>(a, tab, cl_fits(tab), s);
+  return backward_launch<ND, ADAPT, false, false, CellT>(a, 0, cl_fits(0), s);
 }
 
 template <int ND, bool ADAPT>

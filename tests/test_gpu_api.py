@@ -129,3 +129,29 @@ def test_sharded_gradient_equals_full_single_process():
         (out * shard_points(w, r, 4)).sum().backward()
         acc += t_r.grad
     assert rel_l2(acc.cpu().numpy(), t_full.grad.cpu().numpy()) < 1e-5
+
+
+def test_order_cache_reuses_and_invalidates():
+    """The processing order is cached for the same points tensor, recomputed
+    after an in-place change, and never changes results."""
+    from cpab.pytorch import transformer as tr
+    C = cpab((6, 6))
+    pts = torch.from_numpy(rand_points(2, 20000, 31)).to(DEV)
+    th = torch.from_numpy(rand_theta(3, C.params.d, 32)).to(DEV)
+    C.params.__dict__.pop("_order_cache", None)
+    out1 = C.transform_grid(pts, th)
+    o1 = C.params._order_cache[pts.device][1]
+    out2 = C.transform_grid(pts, th)
+    assert C.params._order_cache[pts.device][1] is o1  # reused
+    assert torch.equal(out1, out2)
+    pts.mul_(0.5)  # in place: version counter moves, order is rebuilt
+    out3 = C.transform_grid(pts, th)
+    o3 = C.params._order_cache[pts.device][1]
+    assert o3 is not o1
+    # a stale order only changes which thread integrates which point
+    C.params._order_cache[pts.device] = (C.params._order_cache[pts.device][0], o1)
+    out4 = C.transform_grid(pts, th)
+    assert torch.equal(out3, out4)
+    # and an order for the right points is a permutation
+    assert torch.equal(torch.sort(o3.flatten())[0], torch.arange(20000, device=DEV, dtype=torch.int32))
+    assert tr.ORDER_MIN_POINTS <= 20000
