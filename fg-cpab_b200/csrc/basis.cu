@@ -227,19 +227,34 @@ __global__ void k_expm(const float *__restrict__ As, int64_t n, float dT, float 
   for (int k = 0; k < P; ++k) trels[i * P + k] = r[k];
 }
 
-// Dot product of CSR row [k0, k1) with x split over the 32 lanes of a warp:
-// lane l sums products k0 + l, k0 + l + 32, ... with an fmaf chain, an xor
-// butterfly adds the lane partials; every lane returns the sum.  (The CPU
-// oracle restates this order.)
-__device__ __forceinline__ float warp_dot(const int32_t *__restrict__ colidx,
+// Dot products of CSR row [k0, k1) with up to TC vectors x + u * stride
+// (u < nt), split over the 32 lanes of a warp: lane l sums products k0 + l,
+// k0 + l + 32, ... of every vector with an fmaf chain, and an xor butterfly
+// adds the lane partials; every lane returns all sums.  The index and value
+// of a nonzero are loaded once for the TC vectors, and the TC gathers and
+// chains are independent, so a warp keeps TC loads in flight instead of one.
+// (The per-vector order is fixed; the CPU oracle restates it.)
+constexpr int kDotChunk = 8;
+
+template <int TC>
+__device__ __forceinline__ void warp_dots(const int32_t *__restrict__ colidx,
                                           const float *__restrict__ vals, int k0, int k1,
-                                          const float *__restrict__ x) {
-  float sum = 0.0f;
-  for (int k = k0 + (threadIdx.x & 31); k < k1; k += 32)
-    sum = fmaf(__ldg(vals + k), __ldg(x + __ldg(colidx + k)), sum);
+                                          const float *__restrict__ x, int64_t stride, int nt,
+                                          float (&out)[TC]) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  return sum;
+  for (int u = 0; u < TC; ++u) out[u] = 0.0f;
+  for (int k = k0 + (threadIdx.x & 31); k < k1; k += 32) {
+    const float v = __ldg(vals + k);
+    const float *xc = x + __ldg(colidx + k);
+#pragma unroll
+    for (int u = 0; u < TC; ++u)
+      if (u < nt) out[u] = fmaf(v, __ldg(xc + u * stride), out[u]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+    for (int u = 0; u < TC; ++u) out[u] += __shfl_xor_sync(0xffffffffu, out[u], off);
+  }
 }
 
 // A = B theta (and Trels = expm(A dT) when trels != NULL), in one of two
@@ -249,7 +264,7 @@ __device__ __forceinline__ float warp_dot(const int32_t *__restrict__ colidx,
 //     have <= 4 in every row): one thread per (transformation, cell), each row
 //     summed with a sequential fmaf chain;
 //   * otherwise one warp per cell: each row's nonzeros split over the lanes
-//     (warp_dot), lane j keeping transformation t0 + j's entries, then each
+//     (warp_dots), lane j keeping transformation t0 + j's entries, then each
 //     lane computes the exponential, 32 transformations wide.
 // The grid covers nC warps; the sparse mapping strides over nC * n_theta.
 template <int ND>
@@ -302,12 +317,15 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
 #pragma unroll
     for (int r = 0; r < P; ++r) mine[r] = 0.0f;
     const int tn = min(32, n_theta - t0);
-    for (int j = 0; j < tn; ++j) {
-      const float *th = theta + (int64_t)(t0 + j) * d;
+    for (int j0 = 0; j0 < tn; j0 += kDotChunk) {
+      const float *th = theta + (int64_t)(t0 + j0) * d;
 #pragma unroll
       for (int r = 0; r < P; ++r) {
-        const float sum = warp_dot(colidx, vals, k0[r], k1[r], th);
-        if (lane == j) mine[r] = sum;
+        float sums[kDotChunk];
+        warp_dots<kDotChunk>(colidx, vals, k0[r], k1[r], th, d, tn - j0, sums);
+#pragma unroll
+        for (int u = 0; u < kDotChunk; ++u)
+          if (lane == j0 + u) mine[r] = sums[u];
       }
     }
     if (lane < tn) {
@@ -325,7 +343,7 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
 }
 
 // dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].  One warp
-// per basis column j (warp_dot; clustered column indices let the moment
+// per basis column j (warp_dots; clustered column indices let the moment
 // gathers share sectors).  Columns have 16 to 80 nonzeros for zero-boundary
 // bases and up to ~1,700 for general ones.
 __global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_theta,
@@ -337,9 +355,13 @@ __global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_the
   const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (j >= d) return;
   const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
-  for (int t = 0; t < n_theta; ++t) {
-    const float sum = warp_dot(colidx, vals, k0, k1, moments + (int64_t)t * D);
-    if ((threadIdx.x & 31) == 0) dtheta[(int64_t)t * d + j] = sum;
+  const int lane = threadIdx.x & 31;
+  for (int t0 = 0; t0 < n_theta; t0 += kDotChunk) {
+    float sums[kDotChunk];
+    warp_dots<kDotChunk>(colidx, vals, k0, k1, moments + (int64_t)t0 * D, D, n_theta - t0, sums);
+#pragma unroll
+    for (int u = 0; u < kDotChunk; ++u)
+      if (lane == u && t0 + u < n_theta) dtheta[(int64_t)(t0 + u) * d + j] = sums[u];
   }
 }
 

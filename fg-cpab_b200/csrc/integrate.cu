@@ -15,6 +15,7 @@
 //     changes.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 #include <unordered_map>
@@ -485,10 +486,17 @@ int blocks_per_sm(const void *kernel, int threads, size_t smem) {
   return n;
 }
 
-// One resident wave: blocks along x stride over the points of one
-// transformation (blockIdx.y).
+// Blocks along x stride over the points of one transformation (blockIdx.y).
+// The grid is 1 to 4 resident waves: about 6 points per thread per wave.
+// One wave leaves the whole tail to the slowest blocks; more waves let early
+// finishers take new blocks, at the cost of restaging the cell table.
+// Measured (B200, backward): 2d bench 394 -> 387 us at 2 waves; 3D 10^3
+// 3.15 -> 3.09 ms and dense 2D 1.54 -> 1.45 ms at 4 waves; a block per 512
+// points was slower in both.
 dim3 wave_grid(const void *kernel, int threads, size_t smem, int64_t nP, int n_theta) {
-  const int64_t cap = (int64_t)blocks_per_sm(kernel, threads, smem) * device_info().sm_count;
+  const int64_t wave = (int64_t)blocks_per_sm(kernel, threads, smem) * device_info().sm_count;
+  const int64_t per_thread = nP * n_theta / (wave * threads);
+  const int64_t cap = wave * std::min<int64_t>(4, std::max<int64_t>(1, per_thread / 6));
   const int64_t need = (nP + threads - 1) / threads;
   int64_t nbx = cap / n_theta;
   if (nbx < 1) nbx = 1;
