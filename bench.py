@@ -283,6 +283,7 @@ def make_workload(name, rank, world, dev):
                      % (nd, tess, zb, B, shape, scale, "image" if nd == 2 else "volume"),
                      tess, zb, B, 1, "weak", "batch-parallel over %d GPU(s), no collective" % world)
         C = Cpab(tess, zero_boundary=zb)
+        w.fused_data = (shape[0], int(np.prod(shape[1:])))  # channels, input plane
         g = gen(2 + 10 * rank)
         if nd == 2:
             data = torch.rand(B, *shape, generator=g)
@@ -345,9 +346,12 @@ def run_ours(args, rank, world, local):
     w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev)
     default = args.config == "2d"
 
-    # Per-launch timing of the integration kernels, on the stream they run on.
+    # Per-launch timing of the integration kernels, on the stream they run on
+    # (for transform_data the fused resample-integration kernels).
     timings = {"forward": [], "backward": []}
-    orig = {"forward": _native.forward, "backward": _native.backward}
+    fused = getattr(w, "fused_data", None) is not None
+    orig = {"forward": _native.transform_data if fused else _native.forward,
+            "backward": _native.transform_data_backward if fused else _native.backward}
 
     def timed(name):
         def call(*a, **k):
@@ -360,7 +364,10 @@ def run_ours(args, rank, world, local):
             return r
         return call
 
-    _native.forward, _native.backward = timed("forward"), timed("backward")
+    if fused:
+        _native.transform_data, _native.transform_data_backward = timed("forward"), timed("backward")
+    else:
+        _native.forward, _native.backward = timed("forward"), timed("backward")
 
     # Kernels of this library launched inside the timed steps, counted per
     # native call (order_points runs histogram, scan and scatter).
@@ -377,8 +384,8 @@ def run_ours(args, rank, world, local):
 
     for name in kernels_per_call:
         setattr(_native, name, counting(name, getattr(_native, name)))
-    _native.forward = counting("forward", _native.forward)
-    _native.backward = counting("backward", _native.backward)
+    for name in ("forward", "backward", "transform_data", "transform_data_backward"):
+        setattr(_native, name, counting(name, getattr(_native, name)))
 
     resident = {k: v.to(dev) for k, v in host.items()}
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
@@ -457,10 +464,17 @@ def run_ours(args, rank, world, local):
         p = C.params
         nd, ppc = p.ndim, p.params_pr_cell
         # Algorithmic bytes of one backward launch: the points, the upstream
-        # gradient, cell matrices in and moments out (per stage).
+        # gradient, cell matrices in and moments out (per stage).  The fused
+        # transform_data backward reads the saved grid, the output gradient
+        # and the image instead (its points are generated).
         pts_per_launch = pairs_rank // (w.batch * w.stages)
-        bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
-                     + 2 * w.batch * p.nC * ppc) * 4
+        if fused:
+            ch, plane = w.fused_data
+            bwd_bytes = (w.batch * (nd + ch) * pts_per_launch + w.batch * ch * plane
+                         + 2 * w.batch * p.nC * ppc) * 4
+        else:
+            bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
+                         + 2 * w.batch * p.nC * ppc) * 4
         ach = bwd_bytes / (kern["backward"] * 1e-3) / 1e9
         traffic = profiled("traffic_bytes_per_launch") if default else None
         inst = profiled("warp_instructions_per_launch") if default else None
@@ -487,7 +501,9 @@ def run_ours(args, rank, world, local):
             "config": cfg,
             "e2e": {"value": pairs_step / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "roofline": {"bound": "hbm", "kernel": "k_backward (fused adjoint)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "k_backward_mesh (fused resample + adjoint)" if fused
+                         else "k_backward (fused adjoint)",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes_per_launch": bwd_bytes},

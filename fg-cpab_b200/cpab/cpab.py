@@ -11,6 +11,7 @@ from .core.utility import create_dir, get_dir, params
 from .pytorch.interpolation import interpolate
 from .pytorch.transformer import CPAB_transformer as transformer
 from .pytorch.transformer import _CPABFunction, device_basis
+from .pytorch.transform_data import transform_data as fused_transform_data
 
 # GPU device constant (the current CUDA device).
 _DEVICE = torch.device("cuda")
@@ -197,8 +198,13 @@ class Cpab(object):
     def transform_data(self, data, theta, outsize):
         """transform_grid of a uniform meshgrid followed by interpolate.
 
+        2D and 3D run both in one fused kernel each way (same results as the
+        composition); 1D composes transform_grid and interpolate.
+
         Output: [n_batch, n_channels, *outsize]
         """
+        if self.params.ndim in (2, 3):
+            return fused_transform_data(data, theta, self.params, outsize)
         grid = self.uniform_meshgrid(outsize, device=theta.device)
         grid_t = self.transform_grid(grid, theta)
         return self.interpolate(data, grid_t, outsize)

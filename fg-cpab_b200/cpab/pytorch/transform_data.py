@@ -1,0 +1,72 @@
+"""Fused transform_data (2D/3D): transform_grid of the uniform meshgrid and the
+resample in one kernel each way (cpab/cpab.py:306-308 composes
+transform_grid and interpolate; cpab/pytorch/interpolation.py:47-160).
+
+Results equal the composition's: the meshgrid points are the same linspace
+values, the integration and resample arithmetic are the same device code, and
+the backward starts the adjoint from the resample's grid gradient exactly as
+the composed autograd graph does.  Differentiable in theta and data.
+"""
+import torch
+
+from .. import _native
+from .transformer import _nc, device_basis
+
+
+def mesh_axes(params, outsize, device):
+    """The linspace vectors uniform_meshgrid meshes, concatenated (cached)."""
+    cache = params.__dict__.setdefault("_mesh_axes", {})
+    key = (tuple(int(s) for s in outsize), str(device))
+    hit = cache.get(key)
+    if hit is None:
+        hit = torch.cat([torch.linspace(params.domain_min[i], params.domain_max[i], int(n),
+                                        device=device)
+                         for i, n in enumerate(outsize)]).contiguous()
+        cache[key] = hit
+    return hit
+
+
+def transform_data(data, theta, params, outsize):
+    """[n_batch, C, *outsize] resample of data on the transformed meshgrid."""
+    outsize = tuple(int(s) for s in outsize)
+    nd = params.ndim
+    if nd not in (2, 3):
+        raise ValueError("the fused transform_data supports 2D and 3D")
+    if len(outsize) != nd or data.dim() != nd + 2:
+        raise ValueError("data must be [n_batch, C, *in_size] and outsize have %d entries" % nd)
+    if theta.dim() != 2 or theta.shape[1] != params.d or data.shape[0] != theta.shape[0]:
+        raise ValueError("theta must be [n_batch, %d] with n_batch = data.shape[0]" % params.d)
+    return _TransformData.apply(data, theta, params, outsize)
+
+
+class _TransformData(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, data, theta, params, outsize):
+        nd = params.ndim
+        T = int(params.nstepsolver)
+        adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
+        basis = device_basis(params, theta.device)
+        As, trels = _native.build_A(nd, int(params.nC), basis, theta.contiguous(), 1.0 / T)
+        axes = mesh_axes(params, outsize, theta.device)
+        data_c = data.contiguous()
+        out, grid_t = _native.transform_data(nd, _nc(params), outsize, axes, trels, As, T,
+                                             adaptive, data_c)
+        ctx.params, ctx.outsize, ctx.T, ctx.adaptive = params, outsize, T, adaptive
+        ctx.save_for_backward(data_c, As, grid_t, axes)
+        return out
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad):
+        data, As, grid_t, axes = ctx.saved_tensors
+        want_data, want_theta = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (want_data or want_theta):
+            return None, None, None, None
+        params = ctx.params
+        moments, gd = _native.transform_data_backward(
+            params.ndim, _nc(params), ctx.outsize, axes, As, ctx.T, ctx.adaptive, data, grid_t,
+            grad.contiguous(), want_data)
+        grad_theta = (_native.project(device_basis(params, As.device), moments)
+                      if want_theta else None)
+        return gd, grad_theta, None, None

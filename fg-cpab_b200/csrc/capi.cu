@@ -278,9 +278,101 @@ int check_resample(const char *fn, int ndim, const float *data, int n_batch, int
   return CPAB_OK;
 }
 
+// Checks of the fused transform_data calls; fills `a` (integration over the
+// meshgrid) and `m`.
+int check_mesh(const char *fn, int ndim, const int32_t *nc, const int64_t *out_size,
+               const float *mesh_axes, const float *As, int n_theta, int nstepsolver,
+               int adaptive, const float *data, int n_channels, const int64_t *in_size,
+               const float *grid_t, cpab::IntegrateArgs &a, cpab::MeshArgs &m) {
+  if (ndim != 2 && ndim != 3)
+    return fail(CPAB_ERR_ARG, "%s: ndim must be 2 or 3, got %d", fn, ndim);
+  if (out_size == nullptr || in_size == nullptr) return fail(CPAB_ERR_ARG, "%s: null sizes", fn);
+  int64_t P = 1, plane = 1;
+  for (int k = 0; k < ndim; ++k) {
+    if (out_size[k] < 0) return fail(CPAB_ERR_ARG, "%s: negative output size", fn);
+    if (in_size[k] < 1) return fail(CPAB_ERR_ARG, "%s: input sizes must be positive", fn);
+    if (in_size[k] > (1 << 24))
+      return fail(CPAB_ERR_SIZE, "%s: input axis %d longer than 2^24", fn, k);
+    P *= out_size[k];
+    plane *= in_size[k];
+  }
+  if (P >= ((int64_t)1 << 31))
+    return fail(CPAB_ERR_SIZE, "%s: 2^31 or more output points", fn);
+  if (plane >= ((int64_t)1 << 31))
+    return fail(CPAB_ERR_SIZE, "%s: one input channel has 2^31 or more elements", fn);
+  if (n_channels < 0) return fail(CPAB_ERR_ARG, "%s: negative channel count", fn);
+  // The meshgrid is shared by all transformations: not batched.
+  int st = check_integrate(fn, ndim, nc, mesh_axes, P, 0, As, n_theta, nstepsolver, adaptive, a);
+  if (st != CPAB_OK) return st;
+  if (P > 0 && n_theta > 0 && (grid_t == nullptr || (n_channels > 0 && data == nullptr)))
+    return fail(CPAB_ERR_ARG, "%s: null grid_t or data", fn);
+  a.points = nullptr;
+  m = cpab::MeshArgs{};
+  for (int k = 0; k < 3; ++k) {
+    m.out_size[k] = k < ndim ? out_size[k] : 1;
+    m.in_size[k] = k < ndim ? (int)in_size[k] : 1;
+  }
+  m.axes = mesh_axes;
+  m.data = data;
+  m.C = n_channels;
+  m.grid_t = const_cast<float *>(grid_t);
+  return CPAB_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_size,
+                             const float *mesh_axes, const float *trels, const float *As,
+                             int n_theta, int nstepsolver, int adaptive, const float *data,
+                             int n_channels, const int64_t *in_size, float *grid_t, float *out,
+                             cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  cpab::MeshArgs m;
+  int st = check_mesh("transform_data", ndim, nc, out_size, mesh_axes, As, n_theta, nstepsolver,
+                      adaptive, data, n_channels, in_size, grid_t, a, m);
+  if (st != CPAB_OK) return st;
+  if (n_theta == 0 || a.nP == 0) return ok();
+  if (trels == nullptr || !aligned16(trels))
+    return fail(CPAB_ERR_ARG, "transform_data: trels must be non-null and 16-byte aligned");
+  if (out == nullptr && n_channels > 0) return fail(CPAB_ERR_ARG, "transform_data: null output");
+  a.trels = trels;
+  m.out = out;
+  return cuda_status(cpab::launch_transform_data(a, m, stream), "transform_data");
+}
+
+int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t *out_size,
+                                      const float *mesh_axes, const float *As, int n_theta,
+                                      int nstepsolver, int adaptive, const float *data,
+                                      int n_channels, const int64_t *in_size,
+                                      const float *grid_t, const float *grad_out,
+                                      float *moments, float *grad_data, cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  cpab::MeshArgs m;
+  int st = check_mesh("transform_data_backward", ndim, nc, out_size, mesh_axes, As, n_theta,
+                      nstepsolver, adaptive, data, n_channels, in_size, grid_t, a, m);
+  if (st != CPAB_OK) return st;
+  if (n_theta == 0) return ok();
+  if (moments == nullptr || !aligned16(moments))
+    return fail(CPAB_ERR_ARG, "transform_data_backward: moments must be non-null and 16-byte aligned");
+  if (grad_out == nullptr && a.nP > 0 && n_channels > 0)
+    return fail(CPAB_ERR_ARG, "transform_data_backward: null grad_out");
+  const size_t mbytes = (size_t)n_theta * a.nC * ndim * (ndim + 1) * sizeof(float);
+  cudaError_t e = cudaMemsetAsync(moments, 0, mbytes, stream);
+  if (e != cudaSuccess) return cuda_status(e, "transform_data_backward: clearing moments");
+  if (grad_data != nullptr) {
+    int64_t vol = 1;
+    for (int k = 0; k < ndim; ++k) vol *= in_size[k];
+    e = cudaMemsetAsync(grad_data, 0, (size_t)n_theta * n_channels * vol * sizeof(float), stream);
+    if (e != cudaSuccess) return cuda_status(e, "transform_data_backward: clearing grad_data");
+  }
+  if (a.nP == 0 || n_channels == 0) return ok();  // zero upstream gradient
+  m.grad_out = grad_out;
+  m.grad_data = grad_data;
+  a.moments = moments;
+  return cuda_status(cpab::launch_transform_data_backward(a, m, stream), "transform_data_backward");
+}
 
 int cpab_b200_interpolate(int ndim, const float *data, int n_batch, int n_channels,
                           const int64_t *in_size, const float *grid, const int64_t *out_size,

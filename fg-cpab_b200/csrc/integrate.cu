@@ -21,6 +21,7 @@
 #include <unordered_map>
 
 #include "launch.h"
+#include "resample_device.cuh"
 
 namespace cpab {
 
@@ -42,6 +43,107 @@ constexpr size_t kBwdSmemBudget = 110 * 1024;
 __device__ __forceinline__ int64_t point_of(const int32_t *__restrict__ order, int64_t i) {
   return order ? (int64_t)__ldg(order + i) : i;
 }
+
+// Where the integration kernels' points come from and where results go.
+//   count()         points per transformation
+//   item(slot)      point handled by thread slot `slot`
+//   start(i, p)     initial position
+//   finish(i, p)    forward: consume the integrated position
+//   lambda(i, lam)  backward: adjoint at t = 1 (the upstream gradient)
+//   grad(i, lam)    backward: consume lambda(0)
+
+// transform_grid: points [ndim, nP] (or batched), results [n_theta, ndim, nP].
+template <int ND> struct PointSrc {
+  const float *pin;
+  float *pout;
+  const int32_t *ord;
+  int64_t nP;
+  const float *gin;
+  float *gp;
+  __device__ PointSrc(const IntegrateArgs &a, int b)
+      : pin(a.points + (a.batched ? (int64_t)b * ND * a.nP : 0)),
+        pout(a.out ? a.out + (int64_t)b * ND * a.nP : nullptr),
+        ord(a.order ? a.order + (a.batched ? (int64_t)b * a.nP : 0) : nullptr),
+        nP(a.nP),
+        gin(a.grad_out ? a.grad_out + (int64_t)b * ND * a.nP : nullptr),
+        gp(a.grad_points ? a.grad_points + (int64_t)b * ND * a.nP : nullptr) {}
+  __device__ int64_t count() const { return nP; }
+  __device__ int64_t item(int64_t slot) const { return point_of(ord, slot); }
+  __device__ void start(int64_t i, float (&p)[ND]) const {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+  }
+  __device__ void finish(int64_t i, const float (&p)[ND]) const {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) pout[k * nP + i] = p[k];
+  }
+  __device__ void lambda(int64_t i, float (&lam)[ND]) const {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) lam[k] = __ldg(gin + k * nP + i);
+  }
+  __device__ void grad(int64_t i, const float (&lam)[ND]) const {
+    if (gp) {
+#pragma unroll
+      for (int k = 0; k < ND; ++k) gp[k * nP + i] = lam[k];
+    }
+  }
+};
+
+// transform_data (2D/3D): the uniform meshgrid of out_size in output order;
+// forward writes the integrated grid and resamples every channel of data at
+// it (cpab/cpab.py:306-308 = transform_grid then interpolate); backward forms
+// the upstream gradient from the resample gradient at the saved grid, as the
+// unfused autograd graph does (GD: also scatter grad_data).
+template <int ND, bool GD> struct MeshSrc {
+  const MeshArgs &m;
+  int64_t P, bc0, plane;
+  float *gt;
+  int in[3];
+  __device__ MeshSrc(const IntegrateArgs &a, const MeshArgs &m_, int b) : m(m_) {
+    P = m.out_size[0] * m.out_size[1] * (ND == 3 ? m.out_size[2] : 1);
+    bc0 = (int64_t)b * m.C;
+    plane = (int64_t)m.in_size[0] * m.in_size[1] * (ND == 3 ? m.in_size[2] : 1);
+    gt = m.grid_t + (int64_t)b * ND * P;
+    in[0] = m.in_size[0];
+    in[1] = m.in_size[1];
+    in[2] = m.in_size[2];
+  }
+  __device__ int64_t count() const { return P; }
+  __device__ int64_t item(int64_t slot) const { return slot; }
+  __device__ void start(int64_t o, float (&p)[ND]) const {
+    const int n1 = (int)m.out_size[1];
+    const float *ax = m.axes;
+    if constexpr (ND == 2) {
+      const int i0 = (int)(o / n1), i1 = (int)(o - (int64_t)i0 * n1);
+      p[0] = __ldg(ax + i0);
+      p[1] = __ldg(ax + m.out_size[0] + i1);
+    } else {
+      const int n2 = (int)m.out_size[2];
+      const int64_t r = o / n2;
+      const int i2 = (int)(o - r * n2), i0 = (int)(r / n1), i1 = (int)(r - (int64_t)i0 * n1);
+      p[0] = __ldg(ax + i0);
+      p[1] = __ldg(ax + m.out_size[0] + i1);
+      p[2] = __ldg(ax + m.out_size[0] + m.out_size[1] + i2);
+    }
+  }
+  __device__ void finish(int64_t o, const float (&p)[ND]) const {
+#pragma unroll
+    for (int k = 0; k < ND; ++k) gt[k * P + o] = p[k];
+    const rs::Corners<ND> cr = rs::corners<ND>(p, in);
+    rs::point_fwd<ND>(m.data, m.out, m.C, bc0, plane, P, o, cr);
+  }
+  __device__ void lambda(int64_t o, float (&lam)[ND]) const {
+    float g[ND];
+#pragma unroll
+    for (int k = 0; k < ND; ++k) g[k] = __ldg(gt + k * P + o);
+    const rs::Corners<ND> cr = rs::corners<ND>(g, in);
+    float gw[ND];
+    rs::point_bwd<ND, GD>(m.data, m.grad_out, m.grad_data, m.C, bc0, plane, P, o, cr, gw);
+#pragma unroll
+    for (int k = 0; k < ND; ++k) lam[k] = __fmul_rn(gw[k], (float)(in[k] - 1));
+  }
+  __device__ void grad(int64_t, const float (&)[ND]) const {}
+};
 
 // ---------------------------------------------------------------------------
 // 1D closed form.  cpab/core/cpab_ops_1d.cu:103-205.
@@ -131,8 +233,8 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_1d(IntegrateArgs a) {
 // cpab/core/cpab_ops_2d.cu:212-278, cpab/core/cpab_ops_3d.cu:169-241.
 // ---------------------------------------------------------------------------
 
-template <int ND, bool ADAPT, bool SMEM>
-__global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
+template <int ND, bool ADAPT, bool SMEM, class Src>
+__device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
@@ -147,16 +249,12 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
   const Tess t = a.tess;
   const int T = a.T;
   const float h_half = 0.5f * (1.0f / (float)T);
-  const int64_t nP = a.nP;
-  const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
-  float *pout = a.out + (int64_t)b * ND * nP;
-  const int32_t *ord = a.order ? a.order + (a.batched ? (int64_t)b * nP : 0) : nullptr;
+  const int64_t nP = src.count();
   for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
        slot += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = point_of(ord, slot);
+    const int64_t i = src.item(slot);
     float p[ND];
-#pragma unroll
-    for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+    src.start(i, p);
 #pragma unroll 2
     for (int n = 0; n < T; ++n) {
       const int c = lookup<ND>(t, p);
@@ -180,9 +278,18 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
 #pragma unroll
       for (int k = 0; k < ND; ++k) p[k] = q[k];
     }
-#pragma unroll
-    for (int k = 0; k < ND; ++k) pout[k * nP + i] = p[k];
+    src.finish(i, p);
   }
+}
+
+template <int ND, bool ADAPT, bool SMEM>
+__global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
+  forward_body<ND, ADAPT, SMEM>(a, PointSrc<ND>(a, blockIdx.y));
+}
+
+template <int ND, bool ADAPT, bool SMEM>
+__global__ void __launch_bounds__(kFwdThreads) k_forward_mesh(IntegrateArgs a, MeshArgs m) {
+  forward_body<ND, ADAPT, SMEM>(a, MeshSrc<ND, false>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------
@@ -201,9 +308,8 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
 // (a warp's 32 entries of one step are 64 contiguous bytes), instead of in
 // each thread's local memory, whose ~200 bytes per thread across ~150k
 // resident threads overflow L1 into L2 and DRAM.
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT>
-__global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
-    k_backward(IntegrateArgs a) {
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT, class Src>
+__device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   constexpr int S = kSegSteps;
   extern __shared__ float4 smem4[];
@@ -232,18 +338,13 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
   const float hh = h_half * h;
   const int nfull = T / S;         // full segments of S steps
   const int rem = T - nfull * S;   // steps in the tail segment (0 = none)
-  const int64_t nP = a.nP;
-  const float *pin = a.points + (a.batched ? (int64_t)b * ND * nP : 0);
-  const float *gin = a.grad_out + (int64_t)b * ND * nP;
-  float *gp = a.grad_points ? a.grad_points + (int64_t)b * ND * nP : nullptr;
-  const int32_t *ord = a.order ? a.order + (a.batched ? (int64_t)b * nP : 0) : nullptr;
+  const int64_t nP = src.count();
 
   for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
        slot += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = point_of(ord, slot);
+    const int64_t i = src.item(slot);
     float p[ND];
-#pragma unroll
-    for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+    src.start(i, p);
 
     // Phase 1: midpoint replay, keeping the start of every segment and (for
     // the plain midpoint rule) every step's cell, so that phase 2 replays a
@@ -280,8 +381,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
 
     // Phase 2: segments last to first; replay into registers, then walk back.
     float lam[ND];
-#pragma unroll
-    for (int k = 0; k < ND; ++k) lam[k] = __ldg(gin + k * nP + i);
+    src.lambda(i, lam);
     float mo[P];
 #pragma unroll
     for (int k = 0; k < P; ++k) mo[k] = 0.0f;
@@ -325,10 +425,7 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
     if (rem) phase2(nfull, std::true_type{});
     for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
     if (prev >= 0) flush(prev, mo);
-    if (gp) {
-#pragma unroll
-      for (int k = 0; k < ND; ++k) gp[k * nP + i] = lam[k];
-    }
+    src.grad(i, lam);
   }
 
   if constexpr (M_SMEM) {
@@ -338,6 +435,19 @@ __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBloc
       if (v != 0.0f) atomicAdd(gm + i, v);
     }
   }
+}
+
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT>
+__global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
+    k_backward(IntegrateArgs a) {
+  backward_body<ND, ADAPT, A_SMEM, M_SMEM, CL_SMEM, CellT>(a, PointSrc<ND>(a, blockIdx.y));
+}
+
+// Fused transform_data backward; GD: also the data gradient.
+template <int ND, bool ADAPT, bool A_SMEM, bool CL_SMEM, typename CellT, bool GD>
+__global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
+    k_backward_mesh(IntegrateArgs a, MeshArgs m) {
+  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT>(a, MeshSrc<ND, GD>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------
@@ -505,6 +615,15 @@ dim3 wave_grid(const void *kernel, int threads, size_t smem, int64_t nP, int n_t
 }
 
 template <typename K>
+cudaError_t launch_wave_args(K kernel, int threads, size_t smem, const IntegrateArgs &a,
+                             const MeshArgs &m, cudaStream_t s) {
+  const void *kp = reinterpret_cast<const void *>(kernel);
+  const dim3 grid = wave_grid(kp, threads, smem, a.nP, a.n_theta);
+  kernel<<<grid, threads, smem, s>>>(a, m);
+  return cudaGetLastError();
+}
+
+template <typename K>
 cudaError_t launch_wave(K kernel, int threads, size_t smem, const IntegrateArgs &a,
                         cudaStream_t s) {
   const void *kp = reinterpret_cast<const void *>(kernel);
@@ -550,6 +669,43 @@ cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   if (tab <= kBwdSmemBudget)
     return backward_launch<ND, ADAPT, true, false, CellT>(a, tab, cl_fits(tab), s);
   return backward_launch<ND, ADAPT, false, false, CellT>(a, 0, cl_fits(0), s);
+}
+
+// Fused transform_data launches (2D/3D): same shared-memory choices as the
+// transform_grid kernels.
+template <int ND, bool ADAPT>
+cudaError_t mesh_forward_nd(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s) {
+  const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  if (tab <= kFwdSmemBudget)
+    return launch_wave_args(k_forward_mesh<ND, ADAPT, true>, kFwdThreads, tab, a, m, s);
+  return launch_wave_args(k_forward_mesh<ND, ADAPT, false>, kFwdThreads, 0, a, m, s);
+}
+
+template <int ND, bool ADAPT, typename CellT, bool GD>
+cudaError_t mesh_backward_cells(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s) {
+  const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  constexpr int kT = BwdShape<ND>::kThreads;
+  constexpr bool kCl = !ADAPT && sizeof(CellT) == 2;
+  const size_t cl = kCl ? (size_t)kT * a.T * sizeof(CellT) : 0;
+  if (tab <= kBwdSmemBudget) {
+    if constexpr (kCl) {
+      if (tab + cl <= kBwdSmemBudget)
+        return launch_wave_args(k_backward_mesh<ND, ADAPT, true, true, CellT, GD>, kT, tab + cl,
+                                a, m, s);
+    }
+    return launch_wave_args(k_backward_mesh<ND, ADAPT, true, false, CellT, GD>, kT, tab, a, m, s);
+  }
+  if constexpr (kCl) {
+    if (cl <= kBwdSmemBudget)
+      return launch_wave_args(k_backward_mesh<ND, ADAPT, false, true, CellT, GD>, kT, cl, a, m, s);
+  }
+  return launch_wave_args(k_backward_mesh<ND, ADAPT, false, false, CellT, GD>, kT, 0, a, m, s);
+}
+
+template <int ND, bool ADAPT, bool GD>
+cudaError_t mesh_backward_nd(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s) {
+  if (ADAPT || a.nC <= 65535) return mesh_backward_cells<ND, ADAPT, uint16_t, GD>(a, m, s);
+  return mesh_backward_cells<ND, ADAPT, int32_t, GD>(a, m, s);
 }
 
 template <int ND, bool ADAPT>
@@ -661,6 +817,25 @@ cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s) {
     case 2: return forward_nd<2>(a, s);
     default: return forward_nd<3>(a, s);
   }
+}
+
+cudaError_t launch_transform_data(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s) {
+  if (a.ndim == 2) return a.adaptive ? mesh_forward_nd<2, true>(a, m, s)
+                                     : mesh_forward_nd<2, false>(a, m, s);
+  return a.adaptive ? mesh_forward_nd<3, true>(a, m, s) : mesh_forward_nd<3, false>(a, m, s);
+}
+
+cudaError_t launch_transform_data_backward(const IntegrateArgs &a, const MeshArgs &m,
+                                           cudaStream_t s) {
+  const bool gd = m.grad_data != nullptr;
+  if (a.ndim == 2) {
+    if (a.adaptive) return gd ? mesh_backward_nd<2, true, true>(a, m, s)
+                              : mesh_backward_nd<2, true, false>(a, m, s);
+    return gd ? mesh_backward_nd<2, false, true>(a, m, s) : mesh_backward_nd<2, false, false>(a, m, s);
+  }
+  if (a.adaptive) return gd ? mesh_backward_nd<3, true, true>(a, m, s)
+                            : mesh_backward_nd<3, true, false>(a, m, s);
+  return gd ? mesh_backward_nd<3, false, true>(a, m, s) : mesh_backward_nd<3, false, false>(a, m, s);
 }
 
 cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s) {

@@ -28,7 +28,25 @@ struct IntegrateArgs {
   const int32_t *order;   // processing order [1 or n_theta, nP] or nullptr
 };
 
+// Fused transform_data: the points are the uniform meshgrid of out_size (axis
+// values given), processed in output order o = i0*n1 + i1 (+ i2 fastest in
+// 3D); the integrated grid is resampled into data's shape in the same kernel.
+struct MeshArgs {
+  int64_t out_size[3];
+  const float *axes;       // meshgrid values: axis 0, then axis 1 (, axis 2)
+  const float *data;       // [n_theta, C, *in_size]
+  int C;
+  int in_size[3];
+  float *grid_t;           // [n_theta, ndim, P] in output order (forward out, backward in)
+  float *out;              // forward: [n_theta, C, P]
+  const float *grad_out;   // backward: [n_theta, C, P]
+  float *grad_data;        // backward, may be null (zeroed by the caller)
+};
+
 // Each returns cudaSuccess or the launch error.
+cudaError_t launch_transform_data(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s);
+cudaError_t launch_transform_data_backward(const IntegrateArgs &a, const MeshArgs &m,
+                                           cudaStream_t s);
 cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_forward_1d(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s);

@@ -204,6 +204,44 @@ int cpab_b200_interpolate_backward(int ndim, const float *data, int n_batch,
                                    const float *grad_out, float *grad_grid,
                                    float *grad_data, cpab_stream_t stream);
 
+/*
+ * Fused transform_data (2D/3D):
+ *   out = interpolate(data, transform_grid(meshgrid, theta), out_size)
+ * in one kernel, for n_theta transformations given by As/trels (as for
+ * cpab_b200_forward).  The meshgrid is the uniform grid of out_size whose
+ * axis values are mesh_axes (out_size[0] values of axis 0, then out_size[1]
+ * of axis 1 [, then axis 2]: the linspace vectors uniform_meshgrid meshes).
+ * data is [n_theta, n_channels, *in_size], out [n_theta, n_channels,
+ * *out_size]; grid_t receives the integrated grid as [n_theta, ndim, P] in
+ * OUTPUT order (P = prod(out_size), last axis fastest), which the backward
+ * needs.  Results equal the unfused composition of cpab_b200_forward and
+ * cpab_b200_interpolate bit for bit.
+ * Replaces cpab/cpab.py:306-308 (transform_grid of uniform_meshgrid, then
+ * interpolate, cpab/pytorch/interpolation.py:47-160); the reference has no
+ * single native counterpart.
+ */
+int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_size,
+                             const float *mesh_axes, const float *trels, const float *As,
+                             int n_theta, int nstepsolver, int adaptive,
+                             const float *data, int n_channels, const int64_t *in_size,
+                             float *grid_t, float *out, cpab_stream_t stream);
+
+/*
+ * Backward of cpab_b200_transform_data: forms the gradient of the resample
+ * with respect to the grid at grid_t (as cpab_b200_interpolate_backward) and
+ * runs the adjoint sweep of cpab_b200_backward from it, in one kernel.
+ * moments (16-byte aligned, zeroed here) as for cpab_b200_backward;
+ * grad_data ([n_theta, n_channels, *in_size], may be NULL) is zeroed and
+ * receives the resample's data gradient.
+ */
+int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t *out_size,
+                                      const float *mesh_axes, const float *As, int n_theta,
+                                      int nstepsolver, int adaptive,
+                                      const float *data, int n_channels,
+                                      const int64_t *in_size, const float *grid_t,
+                                      const float *grad_out, float *moments,
+                                      float *grad_data, cpab_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

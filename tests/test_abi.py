@@ -83,6 +83,33 @@ def test_other_entry_points_validate():
     assert L.cpab_b200_forward_1d_closed_form(P, 10, 0, None, P, 1, 0, P, None) == -1
 
 
+def test_transform_data_entry_points_validate():
+    L = _native.lib()
+    sz = (ctypes.c_int64 * 2)(8, 8)
+    zero = (ctypes.c_int64 * 2)(0, 8)
+    neg = (ctypes.c_int64 * 2)(-1, 8)
+    huge = (ctypes.c_int64 * 2)(1 << 16, 1 << 15)
+    fwd = L.cpab_b200_transform_data
+    bwd = L.cpab_b200_transform_data_backward
+    err = lambda: L.cpab_b200_last_error().decode()  # noqa: E731
+    assert fwd(1, NC2, sz, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "ndim" in err()
+    assert fwd(2, NC2, neg, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1
+    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, P, 1, zero, P, P, None) == -1
+    assert fwd(2, NC2, huge, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -4
+    assert fwd(2, NC2, sz, P, P, P, 1, 0, 0, P, 1, sz, P, P, None) == -2
+    assert fwd(2, NC2, sz, P, P, P, 70000, 50, 0, P, 1, sz, P, P, None) == -4
+    assert fwd(2, NC2, sz, P, None, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "trels" in err()
+    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, P, 1, sz, None, P, None) == -1
+    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, None, 1, sz, P, P, None) == -1
+    assert bwd(2, NC2, sz, P, P, 1, 50, 0, P, 1, sz, P, P, None, None, None) == -1
+    assert "moments" in err()
+    nc3 = (ctypes.c_int32 * 3)(2, 2, 2)
+    sz3, bad3 = (ctypes.c_int64 * 3)(4, 4, 4), (ctypes.c_int64 * 3)(4, 0, 4)
+    assert bwd(3, nc3, sz3, P, P, 1, 50, 0, P, 1, bad3, P, P, P, None, None) == -1
+    # nothing to do: no transformations
+    assert fwd(2, NC2, sz, P, P, P, 0, 50, 0, P, 1, sz, P, P, None) == 0
+
+
 def test_errors_are_per_thread():
     import threading
     L = _native.lib()
