@@ -29,10 +29,10 @@ _SIGNATURES = {
     "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate_backward": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p, _p, _p],
-    "cpab_b200_transform_data": [_c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _p, _c_int,
-                                 _p, _p, _p, _p],
-    "cpab_b200_transform_data_backward": [_c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int, _p,
-                                          _c_int, _p, _p, _p, _p, _p, _p],
+    "cpab_b200_transform_data": [_c_int, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _p,
+                                 _c_int, _p, _p, _p, _p],
+    "cpab_b200_transform_data_backward": [_c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int,
+                                          _p, _c_int, _p, _p, _p, _p, _p, _p],
 }
 
 EXPORTS = tuple(_SIGNATURES) + ("cpab_b200_version", "cpab_b200_max_steps",
@@ -241,9 +241,9 @@ def interpolate_backward(ndim, data, grid, outsize, grad_out, want_grid, want_da
     return gg, gd
 
 
-def transform_data(ndim, nc, outsize, axes, trels, As, nstepsolver, adaptive, data):
+def transform_data(ndim, nc, outsize, axes, trels, As, nstepsolver, adaptive, data, order=None):
     """Fused transform_data: returns (out [n_theta, C, *outsize], grid_t
-    [n_theta, ndim, prod(outsize)] in output order)."""
+    [n_theta, ndim, prod(outsize)] in processing order)."""
     _require(data, "data")
     _require(As, "As")
     _require(trels, "Trels")
@@ -254,14 +254,15 @@ def transform_data(ndim, nc, outsize, axes, trels, As, nstepsolver, adaptive, da
     grid_t = torch.empty((n_theta, ndim, P), device=As.device, dtype=torch.float32)
     with torch.cuda.device(As.device):
         _check(lib().cpab_b200_transform_data(
-            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(trels), _ptr(As), n_theta,
+            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(trels),
+            _ptr(As), n_theta,
             int(nstepsolver), int(adaptive), _ptr(data), C, _i64_array(data.shape[2:]),
             _ptr(grid_t), _ptr(out), _stream(As.device)))
     return out, grid_t
 
 
 def transform_data_backward(ndim, nc, outsize, axes, As, nstepsolver, adaptive, data, grid_t,
-                            grad_out, want_data):
+                            grad_out, want_data, order=None):
     """Returns (moments [n_theta, nC, ppc], grad_data or None)."""
     _require(data, "data")
     _require(As, "As")
@@ -272,7 +273,7 @@ def transform_data_backward(ndim, nc, outsize, axes, As, nstepsolver, adaptive, 
     gd = torch.empty_like(data) if want_data else None
     with torch.cuda.device(As.device):
         _check(lib().cpab_b200_transform_data_backward(
-            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(As), n_theta,
+            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(As), n_theta,
             int(nstepsolver), int(adaptive), _ptr(data), C, _i64_array(data.shape[2:]),
             _ptr(grid_t), _ptr(grad_out), _ptr(moments), _ptr(gd), _stream(As.device)))
     return moments, gd

@@ -281,7 +281,8 @@ int check_resample(const char *fn, int ndim, const float *data, int n_batch, int
 // Checks of the fused transform_data calls; fills `a` (integration over the
 // meshgrid) and `m`.
 int check_mesh(const char *fn, int ndim, const int32_t *nc, const int64_t *out_size,
-               const float *mesh_axes, const float *As, int n_theta, int nstepsolver,
+               const float *mesh_axes, const int32_t *order, const float *As, int n_theta,
+               int nstepsolver,
                int adaptive, const float *data, int n_channels, const int64_t *in_size,
                const float *grid_t, cpab::IntegrateArgs &a, cpab::MeshArgs &m) {
   if (ndim != 2 && ndim != 3)
@@ -313,6 +314,7 @@ int check_mesh(const char *fn, int ndim, const int32_t *nc, const int64_t *out_s
     m.in_size[k] = k < ndim ? (int)in_size[k] : 1;
   }
   m.axes = mesh_axes;
+  m.order = order;
   m.data = data;
   m.C = n_channels;
   m.grid_t = const_cast<float *>(grid_t);
@@ -324,13 +326,15 @@ int check_mesh(const char *fn, int ndim, const int32_t *nc, const int64_t *out_s
 extern "C" {
 
 int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_size,
-                             const float *mesh_axes, const float *trels, const float *As,
+                             const float *mesh_axes, const int32_t *order,
+                             const float *trels, const float *As,
                              int n_theta, int nstepsolver, int adaptive, const float *data,
                              int n_channels, const int64_t *in_size, float *grid_t, float *out,
                              cpab_stream_t stream) {
   cpab::IntegrateArgs a;
   cpab::MeshArgs m;
-  int st = check_mesh("transform_data", ndim, nc, out_size, mesh_axes, As, n_theta, nstepsolver,
+  int st = check_mesh("transform_data", ndim, nc, out_size, mesh_axes, order, As, n_theta,
+                      nstepsolver,
                       adaptive, data, n_channels, in_size, grid_t, a, m);
   if (st != CPAB_OK) return st;
   if (n_theta == 0 || a.nP == 0) return ok();
@@ -343,14 +347,16 @@ int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_siz
 }
 
 int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t *out_size,
-                                      const float *mesh_axes, const float *As, int n_theta,
+                                      const float *mesh_axes, const int32_t *order,
+                                      const float *As, int n_theta,
                                       int nstepsolver, int adaptive, const float *data,
                                       int n_channels, const int64_t *in_size,
                                       const float *grid_t, const float *grad_out,
                                       float *moments, float *grad_data, cpab_stream_t stream) {
   cpab::IntegrateArgs a;
   cpab::MeshArgs m;
-  int st = check_mesh("transform_data_backward", ndim, nc, out_size, mesh_axes, As, n_theta,
+  int st = check_mesh("transform_data_backward", ndim, nc, out_size, mesh_axes, order, As,
+                      n_theta,
                       nstepsolver, adaptive, data, n_channels, in_size, grid_t, a, m);
   if (st != CPAB_OK) return st;
   if (n_theta == 0) return ok();

@@ -45,12 +45,12 @@ __device__ __forceinline__ int64_t point_of(const int32_t *__restrict__ order, i
 }
 
 // Where the integration kernels' points come from and where results go.
-//   count()         points per transformation
-//   item(slot)      point handled by thread slot `slot`
-//   start(i, p)     initial position
-//   finish(i, p)    forward: consume the integrated position
-//   lambda(i, lam)  backward: adjoint at t = 1 (the upstream gradient)
-//   grad(i, lam)    backward: consume lambda(0)
+//   count()               points per transformation
+//   item(slot)            point handled by thread slot `slot`
+//   start(slot, i, p)     initial position
+//   finish(slot, i, p)    forward: consume the integrated position
+//   lambda(slot, i, lam)  backward: adjoint at t = 1 (the upstream gradient)
+//   grad(slot, i, lam)    backward: consume lambda(0)
 
 // transform_grid: points [ndim, nP] (or batched), results [n_theta, ndim, nP].
 template <int ND> struct PointSrc {
@@ -69,19 +69,19 @@ template <int ND> struct PointSrc {
         gp(a.grad_points ? a.grad_points + (int64_t)b * ND * a.nP : nullptr) {}
   __device__ int64_t count() const { return nP; }
   __device__ int64_t item(int64_t slot) const { return point_of(ord, slot); }
-  __device__ void start(int64_t i, float (&p)[ND]) const {
+  __device__ void start(int64_t, int64_t i, float (&p)[ND]) const {
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
   }
-  __device__ void finish(int64_t i, const float (&p)[ND]) const {
+  __device__ void finish(int64_t, int64_t i, const float (&p)[ND]) const {
 #pragma unroll
     for (int k = 0; k < ND; ++k) pout[k * nP + i] = p[k];
   }
-  __device__ void lambda(int64_t i, float (&lam)[ND]) const {
+  __device__ void lambda(int64_t, int64_t i, float (&lam)[ND]) const {
 #pragma unroll
     for (int k = 0; k < ND; ++k) lam[k] = __ldg(gin + k * nP + i);
   }
-  __device__ void grad(int64_t i, const float (&lam)[ND]) const {
+  __device__ void grad(int64_t, int64_t i, const float (&lam)[ND]) const {
     if (gp) {
 #pragma unroll
       for (int k = 0; k < ND; ++k) gp[k * nP + i] = lam[k];
@@ -89,10 +89,11 @@ template <int ND> struct PointSrc {
   }
 };
 
-// transform_data (2D/3D): the uniform meshgrid of out_size in output order;
-// forward writes the integrated grid and resamples every channel of data at
-// it (cpab/cpab.py:306-308 = transform_grid then interpolate); backward forms
-// the upstream gradient from the resample gradient at the saved grid, as the
+// transform_data (2D/3D): the uniform meshgrid of out_size, output point o =
+// order[slot] (or slot: output order); forward writes the integrated grid (at
+// the slot: coalesced) and resamples every channel of data at it
+// (cpab/cpab.py:306-308 = transform_grid then interpolate); backward forms the
+// upstream gradient from the resample gradient at the saved grid, as the
 // unfused autograd graph does (GD: also scatter grad_data).
 template <int ND, bool GD> struct MeshSrc {
   const MeshArgs &m;
@@ -109,8 +110,8 @@ template <int ND, bool GD> struct MeshSrc {
     in[2] = m.in_size[2];
   }
   __device__ int64_t count() const { return P; }
-  __device__ int64_t item(int64_t slot) const { return slot; }
-  __device__ void start(int64_t o, float (&p)[ND]) const {
+  __device__ int64_t item(int64_t slot) const { return point_of(m.order, slot); }
+  __device__ void start(int64_t, int64_t o, float (&p)[ND]) const {
     const int n1 = (int)m.out_size[1];
     const float *ax = m.axes;
     if constexpr (ND == 2) {
@@ -126,23 +127,23 @@ template <int ND, bool GD> struct MeshSrc {
       p[2] = __ldg(ax + m.out_size[0] + m.out_size[1] + i2);
     }
   }
-  __device__ void finish(int64_t o, const float (&p)[ND]) const {
+  __device__ void finish(int64_t slot, int64_t o, const float (&p)[ND]) const {
 #pragma unroll
-    for (int k = 0; k < ND; ++k) gt[k * P + o] = p[k];
+    for (int k = 0; k < ND; ++k) gt[k * P + slot] = p[k];
     const rs::Corners<ND> cr = rs::corners<ND>(p, in);
     rs::point_fwd<ND>(m.data, m.out, m.C, bc0, plane, P, o, cr);
   }
-  __device__ void lambda(int64_t o, float (&lam)[ND]) const {
+  __device__ void lambda(int64_t slot, int64_t o, float (&lam)[ND]) const {
     float g[ND];
 #pragma unroll
-    for (int k = 0; k < ND; ++k) g[k] = __ldg(gt + k * P + o);
+    for (int k = 0; k < ND; ++k) g[k] = __ldg(gt + k * P + slot);
     const rs::Corners<ND> cr = rs::corners<ND>(g, in);
     float gw[ND];
     rs::point_bwd<ND, GD>(m.data, m.grad_out, m.grad_data, m.C, bc0, plane, P, o, cr, gw);
 #pragma unroll
     for (int k = 0; k < ND; ++k) lam[k] = __fmul_rn(gw[k], (float)(in[k] - 1));
   }
-  __device__ void grad(int64_t, const float (&)[ND]) const {}
+  __device__ void grad(int64_t, int64_t, const float (&)[ND]) const {}
 };
 
 // ---------------------------------------------------------------------------
@@ -254,7 +255,7 @@ __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &
        slot += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = src.item(slot);
     float p[ND];
-    src.start(i, p);
+    src.start(slot, i, p);
 #pragma unroll 2
     for (int n = 0; n < T; ++n) {
       const int c = lookup<ND>(t, p);
@@ -278,7 +279,7 @@ __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &
 #pragma unroll
       for (int k = 0; k < ND; ++k) p[k] = q[k];
     }
-    src.finish(i, p);
+    src.finish(slot, i, p);
   }
 }
 
@@ -344,7 +345,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
        slot += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = src.item(slot);
     float p[ND];
-    src.start(i, p);
+    src.start(slot, i, p);
 
     // Phase 1: midpoint replay, keeping the start of every segment and (for
     // the plain midpoint rule) every step's cell, so that phase 2 replays a
@@ -381,7 +382,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
 
     // Phase 2: segments last to first; replay into registers, then walk back.
     float lam[ND];
-    src.lambda(i, lam);
+    src.lambda(slot, i, lam);
     float mo[P];
 #pragma unroll
     for (int k = 0; k < P; ++k) mo[k] = 0.0f;
@@ -425,7 +426,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     if (rem) phase2(nfull, std::true_type{});
     for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
     if (prev >= 0) flush(prev, mo);
-    src.grad(i, lam);
+    src.grad(slot, i, lam);
   }
 
   if constexpr (M_SMEM) {

@@ -37,7 +37,8 @@ struct MeshArgs {
   const float *data;       // [n_theta, C, *in_size]
   int C;
   int in_size[3];
-  float *grid_t;           // [n_theta, ndim, P] in output order (forward out, backward in)
+  const int32_t *order;    // processing order of the output points [P], or nullptr
+  float *grid_t;           // [n_theta, ndim, P] in processing order (forward out, backward in)
   float *out;              // forward: [n_theta, C, P]
   const float *grad_out;   // backward: [n_theta, C, P]
   float *grad_data;        // backward, may be null (zeroed by the caller)

@@ -212,16 +212,20 @@ int cpab_b200_interpolate_backward(int ndim, const float *data, int n_batch,
  * axis values are mesh_axes (out_size[0] values of axis 0, then out_size[1]
  * of axis 1 [, then axis 2]: the linspace vectors uniform_meshgrid meshes).
  * data is [n_theta, n_channels, *in_size], out [n_theta, n_channels,
- * *out_size]; grid_t receives the integrated grid as [n_theta, ndim, P] in
- * OUTPUT order (P = prod(out_size), last axis fastest), which the backward
- * needs.  Results equal the unfused composition of cpab_b200_forward and
- * cpab_b200_interpolate bit for bit.
+ * *out_size] (P = prod(out_size) points, last axis fastest).  order (may be
+ * NULL): a permutation of the P output indices giving the processing order,
+ * e.g. cpab_b200_order_points of the meshgrid in output order; the kernel's
+ * thread slot s handles output point order[s].  grid_t receives the
+ * integrated grid as [n_theta, ndim, P] indexed by slot, which the backward
+ * (given the same order) needs.  Results equal the unfused composition of
+ * cpab_b200_forward and cpab_b200_interpolate bit for bit, whatever the order.
  * Replaces cpab/cpab.py:306-308 (transform_grid of uniform_meshgrid, then
  * interpolate, cpab/pytorch/interpolation.py:47-160); the reference has no
  * single native counterpart.
  */
 int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_size,
-                             const float *mesh_axes, const float *trels, const float *As,
+                             const float *mesh_axes, const int32_t *order,
+                             const float *trels, const float *As,
                              int n_theta, int nstepsolver, int adaptive,
                              const float *data, int n_channels, const int64_t *in_size,
                              float *grid_t, float *out, cpab_stream_t stream);
@@ -235,7 +239,8 @@ int cpab_b200_transform_data(int ndim, const int32_t *nc, const int64_t *out_siz
  * receives the resample's data gradient.
  */
 int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t *out_size,
-                                      const float *mesh_axes, const float *As, int n_theta,
+                                      const float *mesh_axes, const int32_t *order,
+                                      const float *As, int n_theta,
                                       int nstepsolver, int adaptive,
                                       const float *data, int n_channels,
                                       const int64_t *in_size, const float *grid_t,

@@ -92,22 +92,22 @@ def test_transform_data_entry_points_validate():
     fwd = L.cpab_b200_transform_data
     bwd = L.cpab_b200_transform_data_backward
     err = lambda: L.cpab_b200_last_error().decode()  # noqa: E731
-    assert fwd(1, NC2, sz, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "ndim" in err()
-    assert fwd(2, NC2, neg, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1
-    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, P, 1, zero, P, P, None) == -1
-    assert fwd(2, NC2, huge, P, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -4
-    assert fwd(2, NC2, sz, P, P, P, 1, 0, 0, P, 1, sz, P, P, None) == -2
-    assert fwd(2, NC2, sz, P, P, P, 70000, 50, 0, P, 1, sz, P, P, None) == -4
-    assert fwd(2, NC2, sz, P, None, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "trels" in err()
-    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, P, 1, sz, None, P, None) == -1
-    assert fwd(2, NC2, sz, P, P, P, 1, 50, 0, None, 1, sz, P, P, None) == -1
-    assert bwd(2, NC2, sz, P, P, 1, 50, 0, P, 1, sz, P, P, None, None, None) == -1
+    assert fwd(1, NC2, sz, P, None, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "ndim" in err()
+    assert fwd(2, NC2, neg, P, None, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -1
+    assert fwd(2, NC2, sz, P, None, P, P, 1, 50, 0, P, 1, zero, P, P, None) == -1
+    assert fwd(2, NC2, huge, P, None, P, P, 1, 50, 0, P, 1, sz, P, P, None) == -4
+    assert fwd(2, NC2, sz, P, None, P, P, 1, 0, 0, P, 1, sz, P, P, None) == -2
+    assert fwd(2, NC2, sz, P, None, P, P, 70000, 50, 0, P, 1, sz, P, P, None) == -4
+    assert fwd(2, NC2, sz, P, None, None, P, 1, 50, 0, P, 1, sz, P, P, None) == -1 and "trels" in err()
+    assert fwd(2, NC2, sz, P, None, P, P, 1, 50, 0, P, 1, sz, None, P, None) == -1
+    assert fwd(2, NC2, sz, P, None, P, P, 1, 50, 0, None, 1, sz, P, P, None) == -1
+    assert bwd(2, NC2, sz, P, None, P, 1, 50, 0, P, 1, sz, P, P, None, None, None) == -1
     assert "moments" in err()
     nc3 = (ctypes.c_int32 * 3)(2, 2, 2)
     sz3, bad3 = (ctypes.c_int64 * 3)(4, 4, 4), (ctypes.c_int64 * 3)(4, 0, 4)
-    assert bwd(3, nc3, sz3, P, P, 1, 50, 0, P, 1, bad3, P, P, P, None, None) == -1
+    assert bwd(3, nc3, sz3, P, None, P, 1, 50, 0, P, 1, bad3, P, P, P, None, None) == -1
     # nothing to do: no transformations
-    assert fwd(2, NC2, sz, P, P, P, 0, 50, 0, P, 1, sz, P, P, None) == 0
+    assert fwd(2, NC2, sz, P, None, P, P, 0, 50, 0, P, 1, sz, P, P, None) == 0
 
 
 def test_errors_are_per_thread():
