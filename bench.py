@@ -350,8 +350,10 @@ def run_ours(args, rank, world, local):
     # (for transform_data the fused resample-integration kernels).
     timings = {"forward": [], "backward": []}
     fused = getattr(w, "fused_data", None) is not None
-    orig = {"forward": _native.transform_data if fused else _native.forward,
-            "backward": _native.transform_data_backward if fused else _native.backward}
+    chain = w.stages > 1 and C.params.ndim in (2, 3)   # one launch through all stages
+    names = (("transform_data", "transform_data_backward") if fused else
+             ("forward_chain", "backward_chain") if chain else ("forward", "backward"))
+    orig = {"forward": getattr(_native, names[0]), "backward": getattr(_native, names[1])}
 
     def timed(name):
         def call(*a, **k):
@@ -364,10 +366,8 @@ def run_ours(args, rank, world, local):
             return r
         return call
 
-    if fused:
-        _native.transform_data, _native.transform_data_backward = timed("forward"), timed("backward")
-    else:
-        _native.forward, _native.backward = timed("forward"), timed("backward")
+    setattr(_native, names[0], timed("forward"))
+    setattr(_native, names[1], timed("backward"))
 
     # Kernels of this library launched inside the timed steps, counted per
     # native call (order_points runs histogram, scan and scatter).
@@ -384,7 +384,8 @@ def run_ours(args, rank, world, local):
 
     for name in kernels_per_call:
         setattr(_native, name, counting(name, getattr(_native, name)))
-    for name in ("forward", "backward", "transform_data", "transform_data_backward"):
+    for name in ("forward", "backward", "transform_data", "transform_data_backward",
+                 "forward_chain", "backward_chain"):
         setattr(_native, name, counting(name, getattr(_native, name)))
 
     resident = {k: v.to(dev) for k, v in host.items()}
@@ -472,6 +473,11 @@ def run_ours(args, rank, world, local):
             ch, plane = w.fused_data
             bwd_bytes = (w.batch * (nd + ch) * pts_per_launch + w.batch * ch * plane
                          + 2 * w.batch * p.nC * ppc) * 4
+        elif chain:  # all stages: saved stage inputs instead of recomputed ones
+            K = w.stages
+            bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
+                         + (K - 1) * w.batch * nd * pts_per_launch
+                         + 2 * K * w.batch * p.nC * ppc) * 4
         else:
             bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
                          + 2 * w.batch * p.nC * ppc) * 4
@@ -503,6 +509,7 @@ def run_ours(args, rank, world, local):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm",
                          "kernel": "k_backward_mesh (fused resample + adjoint)" if fused
+                         else "k_backward (fused adjoint, all chain stages)" if chain
                          else "k_backward (fused adjoint)",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "peak_kind": peak_kind, "traffic": traffic,

@@ -29,6 +29,10 @@ _SIGNATURES = {
     "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate_backward": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p, _p, _p],
+    "cpab_b200_forward_chain": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _p, _c_int, _c_int,
+                                _c_int, _c_int, _p, _p, _p],
+    "cpab_b200_backward_chain": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _c_int, _c_int, _p, _p,
+                                 _c_int, _c_int, _p, _p, _p],
     "cpab_b200_transform_data": [_c_int, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _p,
                                  _c_int, _p, _p, _p, _p],
     "cpab_b200_transform_data_backward": [_c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int,
@@ -277,3 +281,43 @@ def transform_data_backward(ndim, nc, outsize, axes, As, nstepsolver, adaptive, 
             int(nstepsolver), int(adaptive), _ptr(data), C, _i64_array(data.shape[2:]),
             _ptr(grid_t), _ptr(grad_out), _ptr(moments), _ptr(gd), _stream(As.device)))
     return moments, gd
+
+
+def forward_chain(ndim, nc, points, batched, trels, As, n_stages, nstepsolver, adaptive,
+                  order=None):
+    """Fused chain; trels/As [n_stages * n_theta, nC, ...] stage-major.  Returns
+    (out [n_theta, ndim, nP], stage_points [n_stages-1, n_theta, ndim, nP] or None)."""
+    _require(points, "points")
+    _require(As, "As")
+    _require(trels, "Trels")
+    n_theta = As.shape[0] // n_stages
+    nP = points.shape[-1]
+    out = torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
+    sp = (torch.empty((n_stages - 1, n_theta, ndim, nP), device=As.device, dtype=torch.float32)
+          if n_stages > 1 else None)
+    with torch.cuda.device(As.device):
+        _check(lib().cpab_b200_forward_chain(
+            ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(trels),
+            _ptr(As), n_stages, n_theta, int(nstepsolver), int(adaptive), _ptr(sp), _ptr(out),
+            _stream(As.device)))
+    return out, sp
+
+
+def backward_chain(ndim, nc, points, batched, As, n_stages, grad_out, stage_points, nstepsolver,
+                   adaptive, want_points, order=None):
+    """Returns (moments [n_stages * n_theta, nC, ppc], grad_points or None)."""
+    _require(points, "points")
+    _require(As, "As")
+    _require(grad_out, "grad")
+    n_theta, nC = As.shape[0] // n_stages, As.shape[1]
+    nP = points.shape[-1]
+    moments = torch.empty((n_stages * n_theta, nC, ndim * (ndim + 1)), device=As.device,
+                          dtype=torch.float32)
+    gp = (torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
+          if want_points else None)
+    with torch.cuda.device(As.device):
+        _check(lib().cpab_b200_backward_chain(
+            ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_stages,
+            n_theta, _ptr(grad_out), _ptr(stage_points), int(nstepsolver), int(adaptive),
+            _ptr(moments), _ptr(gp), _stream(As.device)))
+    return moments, gp

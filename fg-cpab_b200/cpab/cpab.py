@@ -10,7 +10,7 @@ from .core.tesselation import Tesselation1D, Tesselation2D, Tesselation3D
 from .core.utility import create_dir, get_dir, params
 from .pytorch.interpolation import interpolate
 from .pytorch.transformer import CPAB_transformer as transformer
-from .pytorch.transformer import _CPABFunction, device_basis
+from .pytorch.transformer import _CPABFunction, device_basis, transform_chain
 from .pytorch.transform_data import transform_data as fused_transform_data
 
 # GPU device constant (the current CUDA device).
@@ -186,6 +186,9 @@ class Cpab(object):
             assert grid.shape[0] == n_batch, \
                 "When passing a 3D grid, its batch dimension must match theta_chain"
         dt = (1.0 / n_transforms) if scale_by_dt else 1.0
+        if self.params.ndim in (2, 3) and n_transforms > 1:
+            # One kernel through all stages each way (same per-stage arithmetic).
+            return transform_chain(grid, theta_chain * dt, self.params, compute_points_grad=True)
         out = grid
         for i in range(n_transforms):
             out = transformer(out, theta_chain[i] * dt, self.params, compute_points_grad=True)

@@ -166,3 +166,52 @@ class _CPABFunction(torch.autograd.Function):
             if ctx.group is not None:
                 torch.distributed.all_reduce(grad_theta, group=ctx.group)
         return grad_points, grad_theta, None, None, None
+
+
+def transform_chain(points, theta_stages, params, compute_points_grad=False):
+    """Fused transform_grid_chain (2D/3D): theta_stages [n_stages, n_batch, d]
+    (already scaled), applied in order to points in one kernel each way."""
+    assert params.ndim in (2, 3), "the fused chain supports 2D and 3D"
+    return _ChainFunction.apply(points, theta_stages, params, compute_points_grad)
+
+
+class _ChainFunction(torch.autograd.Function):
+    """transform_grid_chain (cpab/cpab.py:269-278): the stages' A/Trels from one
+    build_A call, one forward kernel through all stages, one backward kernel
+    walking the stages back (lambda handed from stage to stage inside it)."""
+
+    @staticmethod
+    def forward(ctx, points, theta_stages, params, compute_points_grad=False):
+        K, nb, d = theta_stages.shape
+        batched, _ = _layout(points, theta_stages[0], params)
+        nd = params.ndim
+        basis = device_basis(params, theta_stages.device)
+        T = int(params.nstepsolver)
+        adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
+        points_c = points.contiguous()
+        As, trels = _native.build_A(nd, int(params.nC), basis,
+                                    theta_stages.reshape(K * nb, d).contiguous(), 1.0 / T)
+        order = _order(params, points_c, batched)
+        out, sp = _native.forward_chain(nd, _nc(params), points_c, batched, trels, As, K, T,
+                                        adaptive, order)
+        ctx.params, ctx.batched, ctx.T, ctx.adaptive = params, batched, T, adaptive
+        ctx.K, ctx.order, ctx.compute_points_grad = K, order, compute_points_grad
+        ctx.save_for_backward(points_c, As, sp)
+        return out
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad):
+        points, As, sp = ctx.saved_tensors
+        params = ctx.params
+        want_points = ctx.compute_points_grad and ctx.needs_input_grad[0]
+        moments, grad_points = _native.backward_chain(
+            params.ndim, _nc(params), points, ctx.batched, As, ctx.K, grad.contiguous(), sp,
+            ctx.T, ctx.adaptive, want_points, ctx.order)
+        if grad_points is not None and points.dim() == 2:
+            grad_points = grad_points.sum(dim=0)
+        grad_theta = None
+        if ctx.needs_input_grad[1]:
+            grad_theta = _native.project(device_basis(params, As.device), moments)
+            grad_theta = grad_theta.reshape(ctx.K, -1, grad_theta.shape[-1])
+        return grad_points, grad_theta, None, None

@@ -197,6 +197,61 @@ int cpab_b200_backward(int ndim, const int32_t *nc, const float *points, int64_t
   return cuda_status(cpab::launch_backward(a, stream), "backward");
 }
 
+int cpab_b200_forward_chain(int ndim, const int32_t *nc, const float *points, int64_t nP,
+                            int points_batched, const int32_t *order, const float *trels,
+                            const float *As, int n_stages, int n_theta, int nstepsolver,
+                            int adaptive, float *stage_points, float *out, cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  int st = check_integrate("forward_chain", ndim, nc, points, nP, points_batched, As, n_theta,
+                           nstepsolver, adaptive, a);
+  if (st != CPAB_OK) return st;
+  if (ndim == 1) return fail(CPAB_ERR_ARG, "forward_chain: ndim must be 2 or 3");
+  if (n_stages < 1 || n_stages > 4096)
+    return fail(CPAB_ERR_ARG, "forward_chain: n_stages must be in [1, 4096], got %d", n_stages);
+  if (nP == 0 || n_theta == 0) return ok();
+  if (trels == nullptr || !aligned16(trels))
+    return fail(CPAB_ERR_ARG, "forward_chain: trels must be non-null and 16-byte aligned");
+  if (out == nullptr || (n_stages > 1 && stage_points == nullptr))
+    return fail(CPAB_ERR_ARG, "forward_chain: null output");
+  a.trels = trels;
+  a.out = out;
+  a.order = order;
+  a.n_stages = n_stages;
+  a.stage_points = stage_points;
+  return cuda_status(cpab::launch_forward(a, stream), "forward_chain");
+}
+
+int cpab_b200_backward_chain(int ndim, const int32_t *nc, const float *points, int64_t nP,
+                             int points_batched, const int32_t *order, const float *As,
+                             int n_stages, int n_theta, const float *grad_out,
+                             const float *stage_points, int nstepsolver, int adaptive,
+                             float *moments, float *grad_points, cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  int st = check_integrate("backward_chain", ndim, nc, points, nP, points_batched, As, n_theta,
+                           nstepsolver, adaptive, a);
+  if (st != CPAB_OK) return st;
+  if (ndim == 1) return fail(CPAB_ERR_ARG, "backward_chain: ndim must be 2 or 3");
+  if (n_stages < 1 || n_stages > 4096)
+    return fail(CPAB_ERR_ARG, "backward_chain: n_stages must be in [1, 4096], got %d", n_stages);
+  if (n_theta == 0) return ok();
+  if (moments == nullptr || !aligned16(moments))
+    return fail(CPAB_ERR_ARG, "backward_chain: moments must be non-null and 16-byte aligned");
+  if (nP > 0 && (grad_out == nullptr || (n_stages > 1 && stage_points == nullptr)))
+    return fail(CPAB_ERR_ARG, "backward_chain: null grad_out or stage_points");
+  const size_t mbytes =
+      (size_t)n_stages * n_theta * a.nC * ndim * (ndim + 1) * sizeof(float);
+  cudaError_t e = cudaMemsetAsync(moments, 0, mbytes, stream);
+  if (e != cudaSuccess) return cuda_status(e, "backward_chain: clearing moments");
+  if (nP == 0) return ok();
+  a.grad_out = grad_out;
+  a.moments = moments;
+  a.grad_points = grad_points;
+  a.order = order;
+  a.n_stages = n_stages;
+  a.stage_points = const_cast<float *>(stage_points);
+  return cuda_status(cpab::launch_backward(a, stream), "backward_chain");
+}
+
 int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points, int64_t nP,
                            int n_sets, int32_t *counts_scratch, int32_t *order,
                            cpab_stream_t stream) {

@@ -48,6 +48,8 @@ __device__ __forceinline__ int64_t point_of(const int32_t *__restrict__ order, i
 //   count()               points per transformation
 //   item(slot)            point handled by thread slot `slot`
 //   start(slot, i, p)     initial position
+//   start_stage(st, ...)  input of chain stage st (stage 0: start)
+//   save_stage(st, ...)   forward: keep the input of chain stage st + 1
 //   finish(slot, i, p)    forward: consume the integrated position
 //   lambda(slot, i, lam)  backward: adjoint at t = 1 (the upstream gradient)
 //   grad(slot, i, lam)    backward: consume lambda(0)
@@ -60,18 +62,33 @@ template <int ND> struct PointSrc {
   int64_t nP;
   const float *gin;
   float *gp;
+  float *sp;          // stage inputs of this transformation, stage 1
+  int64_t sp_stride;  // between stages
   __device__ PointSrc(const IntegrateArgs &a, int b)
       : pin(a.points + (a.batched ? (int64_t)b * ND * a.nP : 0)),
         pout(a.out ? a.out + (int64_t)b * ND * a.nP : nullptr),
         ord(a.order ? a.order + (a.batched ? (int64_t)b * a.nP : 0) : nullptr),
         nP(a.nP),
         gin(a.grad_out ? a.grad_out + (int64_t)b * ND * a.nP : nullptr),
-        gp(a.grad_points ? a.grad_points + (int64_t)b * ND * a.nP : nullptr) {}
+        gp(a.grad_points ? a.grad_points + (int64_t)b * ND * a.nP : nullptr),
+        sp(a.stage_points ? a.stage_points + (int64_t)b * ND * a.nP : nullptr),
+        sp_stride((int64_t)a.n_theta * ND * a.nP) {}
   __device__ int64_t count() const { return nP; }
   __device__ int64_t item(int64_t slot) const { return point_of(ord, slot); }
   __device__ void start(int64_t, int64_t i, float (&p)[ND]) const {
 #pragma unroll
     for (int k = 0; k < ND; ++k) p[k] = __ldg(pin + k * nP + i);
+  }
+  __device__ void start_stage(int st, int64_t slot, int64_t i, float (&p)[ND]) const {
+    if (st == 0) return start(slot, i, p);
+    const float *q = sp + (st - 1) * sp_stride + slot;
+#pragma unroll
+    for (int k = 0; k < ND; ++k) p[k] = q[k * nP];
+  }
+  __device__ void save_stage(int st, int64_t slot, const float (&p)[ND]) const {
+    float *q = sp + st * sp_stride + slot;
+#pragma unroll
+    for (int k = 0; k < ND; ++k) q[k * nP] = p[k];
   }
   __device__ void finish(int64_t, int64_t i, const float (&p)[ND]) const {
 #pragma unroll
@@ -127,6 +144,10 @@ template <int ND, bool GD> struct MeshSrc {
       p[2] = __ldg(ax + m.out_size[0] + m.out_size[1] + i2);
     }
   }
+  __device__ void start_stage(int, int64_t slot, int64_t o, float (&p)[ND]) const {
+    start(slot, o, p);
+  }
+  __device__ void save_stage(int, int64_t, const float (&)[ND]) const {}
   __device__ void finish(int64_t slot, int64_t o, const float (&p)[ND]) const {
 #pragma unroll
     for (int k = 0; k < ND; ++k) gt[k * P + slot] = p[k];
@@ -234,28 +255,32 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_1d(IntegrateArgs a) {
 // cpab/core/cpab_ops_2d.cu:212-278, cpab/core/cpab_ops_3d.cu:169-241.
 // ---------------------------------------------------------------------------
 
-template <int ND, bool ADAPT, bool SMEM, class Src>
+// CHAIN: a.n_stages transformations per point (fused chains; tables are
+// never staged then).  Without it the stage loop compiles away.
+template <int ND, bool ADAPT, bool SMEM, bool CHAIN, class Src>
 __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
   const int b = blockIdx.y;
-  const float *tg = a.trels + (int64_t)b * a.nC * P;
-  const float *ag = a.As + (int64_t)b * a.nC * P;
   if constexpr (SMEM) {
-    stage_table<ND>(s_tab, tg, a.nC);
+    stage_table<ND>(s_tab, a.trels + (int64_t)b * a.nC * P, a.nC);
     __syncthreads();
   }
-  const float *tab = SMEM ? s_tab : tg;
   const Tess t = a.tess;
   const int T = a.T;
   const float h_half = 0.5f * (1.0f / (float)T);
   const int64_t nP = src.count();
+  const int nst = CHAIN ? a.n_stages : 1;
   for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
        slot += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = src.item(slot);
     float p[ND];
     src.start(slot, i, p);
+    for (int st = 0; st < nst; ++st) {
+    const int64_t off = ((int64_t)st * a.n_theta + b) * a.nC * P;
+    const float *tab = SMEM ? s_tab : a.trels + off;
+    const float *ag = a.As + off;
 #pragma unroll 2
     for (int n = 0; n < T; ++n) {
       const int c = lookup<ND>(t, p);
@@ -279,18 +304,20 @@ __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &
 #pragma unroll
       for (int k = 0; k < ND; ++k) p[k] = q[k];
     }
+    if (st + 1 < nst) src.save_stage(st, slot, p);
+    }
     src.finish(slot, i, p);
   }
 }
 
-template <int ND, bool ADAPT, bool SMEM>
+template <int ND, bool ADAPT, bool SMEM, bool CHAIN = false>
 __global__ void __launch_bounds__(kFwdThreads) k_forward(IntegrateArgs a) {
-  forward_body<ND, ADAPT, SMEM>(a, PointSrc<ND>(a, blockIdx.y));
+  forward_body<ND, ADAPT, SMEM, CHAIN>(a, PointSrc<ND>(a, blockIdx.y));
 }
 
 template <int ND, bool ADAPT, bool SMEM>
 __global__ void __launch_bounds__(kFwdThreads) k_forward_mesh(IntegrateArgs a, MeshArgs m) {
-  forward_body<ND, ADAPT, SMEM>(a, MeshSrc<ND, false>(a, m, blockIdx.y));
+  forward_body<ND, ADAPT, SMEM, false>(a, MeshSrc<ND, false>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------
@@ -309,7 +336,8 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_mesh(IntegrateArgs a, M
 // (a warp's 32 entries of one step are 64 contiguous bytes), instead of in
 // each thread's local memory, whose ~200 bytes per thread across ~150k
 // resident threads overflow L1 into L2 and DRAM.
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT, class Src>
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT, bool CHAIN,
+          class Src>
 __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   constexpr int S = kSegSteps;
@@ -326,7 +354,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     for (int i = threadIdx.x; i < nC * P; i += blockDim.x) s_mom[i] = 0.0f;
   }
   if constexpr (A_SMEM || M_SMEM) __syncthreads();
-  const float *tab = A_SMEM ? s_tab : ag;
+  const float *tab = A_SMEM ? s_tab : ag;  // per stage in fused chains
   auto flush = [&](int c, float (&mo)[P]) {
     if constexpr (M_SMEM) flush_smem<P>(s_mom, c, mo);
     else flush_moments<P>(gm, c, mo);
@@ -344,8 +372,17 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
   for (int64_t slot = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; slot < nP;
        slot += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = src.item(slot);
+    float lam[ND];
+    // Fused chains walk the stages backwards, lambda flowing from each stage
+    // into the one before; a single transformation is one stage.
+    const int nst = CHAIN ? a.n_stages : 1;
+    for (int st = nst - 1; st >= 0; --st) {
+    if constexpr (CHAIN) {
+      tab = a.As + ((int64_t)st * a.n_theta + b) * nC * P;
+      gm = a.moments + ((int64_t)st * a.n_theta + b) * nC * P;
+    }
     float p[ND];
-    src.start(slot, i, p);
+    src.start_stage(st, slot, i, p);
 
     // Phase 1: midpoint replay, keeping the start of every segment and (for
     // the plain midpoint rule) every step's cell, so that phase 2 replays a
@@ -381,8 +418,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     if (rem) phase1(nfull, std::true_type{});
 
     // Phase 2: segments last to first; replay into registers, then walk back.
-    float lam[ND];
-    src.lambda(slot, i, lam);
+    if (st == nst - 1) src.lambda(slot, i, lam);
     float mo[P];
 #pragma unroll
     for (int k = 0; k < P; ++k) mo[k] = 0.0f;
@@ -426,6 +462,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     if (rem) phase2(nfull, std::true_type{});
     for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
     if (prev >= 0) flush(prev, mo);
+    }
     src.grad(slot, i, lam);
   }
 
@@ -438,17 +475,19 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
   }
 }
 
-template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT>
+template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT,
+          bool CHAIN = false>
 __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
     k_backward(IntegrateArgs a) {
-  backward_body<ND, ADAPT, A_SMEM, M_SMEM, CL_SMEM, CellT>(a, PointSrc<ND>(a, blockIdx.y));
+  backward_body<ND, ADAPT, A_SMEM, M_SMEM, CL_SMEM, CellT, CHAIN>(a, PointSrc<ND>(a, blockIdx.y));
 }
 
 // Fused transform_data backward; GD: also the data gradient.
 template <int ND, bool ADAPT, bool A_SMEM, bool CL_SMEM, typename CellT, bool GD>
 __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
     k_backward_mesh(IntegrateArgs a, MeshArgs m) {
-  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT>(a, MeshSrc<ND, GD>(a, m, blockIdx.y));
+  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT, false>(a,
+                                                                MeshSrc<ND, GD>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------
@@ -604,9 +643,10 @@ int blocks_per_sm(const void *kernel, int threads, size_t smem) {
 // Measured (B200, backward): 2d bench 394 -> 387 us at 2 waves; 3D 10^3
 // 3.15 -> 3.09 ms and dense 2D 1.54 -> 1.45 ms at 4 waves; a block per 512
 // points was slower in both.
-dim3 wave_grid(const void *kernel, int threads, size_t smem, int64_t nP, int n_theta) {
+dim3 wave_grid(const void *kernel, int threads, size_t smem, int64_t nP, int n_theta,
+               int n_stages = 1) {
   const int64_t wave = (int64_t)blocks_per_sm(kernel, threads, smem) * device_info().sm_count;
-  const int64_t per_thread = nP * n_theta / (wave * threads);
+  const int64_t per_thread = nP * n_theta * n_stages / (wave * threads);
   const int64_t cap = wave * std::min<int64_t>(4, std::max<int64_t>(1, per_thread / 6));
   const int64_t need = (nP + threads - 1) / threads;
   int64_t nbx = cap / n_theta;
@@ -628,7 +668,7 @@ template <typename K>
 cudaError_t launch_wave(K kernel, int threads, size_t smem, const IntegrateArgs &a,
                         cudaStream_t s) {
   const void *kp = reinterpret_cast<const void *>(kernel);
-  const dim3 grid = wave_grid(kp, threads, smem, a.nP, a.n_theta);
+  const dim3 grid = wave_grid(kp, threads, smem, a.nP, a.n_theta, a.n_stages);
   kernel<<<grid, threads, smem, s>>>(a);
   return cudaGetLastError();
 }
@@ -636,6 +676,11 @@ cudaError_t launch_wave(K kernel, int threads, size_t smem, const IntegrateArgs 
 template <int ND>
 cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  if constexpr (ND > 1) {
+    if (a.n_stages > 1)  // fused chain: tables read through L1/L2
+      return a.adaptive ? launch_wave(k_forward<ND, true, false, true>, kFwdThreads, 0, a, s)
+                        : launch_wave(k_forward<ND, false, false, true>, kFwdThreads, 0, a, s);
+  }
   const bool smem = tab <= kFwdSmemBudget;
   if (a.adaptive) {
     return smem ? launch_wave(k_forward<ND, true, true>, kFwdThreads, tab, a, s)
@@ -655,6 +700,17 @@ cudaError_t backward_launch(const IntegrateArgs &a, size_t smem, size_t cl, cuda
   return launch_wave(k_backward<ND, ADAPT, A_SMEM, M_SMEM, false, CellT>, kT, smem, a, s);
 }
 
+// Fused chains: tables stay in global memory (stage after stage per thread).
+template <int ND, bool ADAPT, typename CellT>
+cudaError_t backward_chain_launch(const IntegrateArgs &a, size_t cl, cudaStream_t s) {
+  constexpr int kT = BwdShape<ND>::kThreads;
+  if constexpr (!ADAPT && sizeof(CellT) == 2) {
+    if (cl > 0)
+      return launch_wave(k_backward<ND, ADAPT, false, false, true, CellT, true>, kT, cl, a, s);
+  }
+  return launch_wave(k_backward<ND, ADAPT, false, false, false, CellT, true>, kT, 0, a, s);
+}
+
 template <int ND, bool ADAPT, typename CellT>
 cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
@@ -666,6 +722,9 @@ cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   if constexpr (ND == 1) {
     if (2 * tab <= kBwdSmemBudget)
       return backward_launch<ND, ADAPT, true, true, CellT>(a, 2 * tab, cl_fits(2 * tab), s);
+  }
+  if constexpr (ND > 1) {
+    if (a.n_stages > 1) return backward_chain_launch<ND, ADAPT, CellT>(a, cl_fits(0), s);
   }
   if (tab <= kBwdSmemBudget)
     return backward_launch<ND, ADAPT, true, false, CellT>(a, tab, cl_fits(tab), s);

@@ -26,6 +26,13 @@ struct IntegrateArgs {
   float *moments;         // backward: [n_theta, nC, ppc]
   float *grad_points;     // backward: [n_theta, ndim, nP] or nullptr
   const int32_t *order;   // processing order [1 or n_theta, nP] or nullptr
+  // Fused chains (2D/3D): n_stages transformations applied in sequence to
+  // every point.  trels, As and moments are then [n_stages, n_theta, nC, ppc];
+  // stage_points holds the inputs of stages 1..n_stages-1 as
+  // [n_stages-1, n_theta, ndim, nP] indexed by processing slot (written by the
+  // forward, read by the backward with the same order).
+  int n_stages = 1;
+  float *stage_points = nullptr;
 };
 
 // Fused transform_data: the points are the uniform meshgrid of out_size (axis

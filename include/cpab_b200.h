@@ -205,6 +205,39 @@ int cpab_b200_interpolate_backward(int ndim, const float *data, int n_batch,
                                    float *grad_data, cpab_stream_t stream);
 
 /*
+ * Fused chain (2D/3D): n_stages transformations applied in sequence to every
+ * point in one kernel -- transform_grid_chain (cpab/cpab.py:269-278) without
+ * the per-stage launches and intermediate tensors.  trels and As are
+ * [n_stages, n_theta, nC, ndim, ndim+1] (stage-major; cpab_b200_build_A over
+ * n_stages * n_theta rows of theta produces this layout).  points as for
+ * cpab_b200_forward (stage 0 input); out [n_theta, ndim, nP] is the last
+ * stage's output.  stage_points ([n_stages-1, n_theta, ndim, nP], may be NULL
+ * when n_stages = 1) receives the inputs of stages 1.. indexed by processing
+ * slot (order[s] when order != NULL); the backward needs them and the same
+ * order.  Each stage's arithmetic is exactly cpab_b200_forward's.
+ */
+int cpab_b200_forward_chain(int ndim, const int32_t *nc, const float *points,
+                            int64_t nP, int points_batched, const int32_t *order,
+                            const float *trels, const float *As, int n_stages,
+                            int n_theta, int nstepsolver, int adaptive,
+                            float *stage_points, float *out, cpab_stream_t stream);
+
+/*
+ * Backward of cpab_b200_forward_chain: the adjoint sweeps of all stages, last
+ * to first, lambda flowing from each stage into the previous one (the
+ * gradient the reference's autograd passes between its per-stage
+ * backward_moments_and_points calls).  moments (16-byte aligned, zeroed
+ * here) is [n_stages, n_theta, nC, ppc]; grad_points as for
+ * cpab_b200_backward (lambda at the chain input), may be NULL.
+ */
+int cpab_b200_backward_chain(int ndim, const int32_t *nc, const float *points,
+                             int64_t nP, int points_batched, const int32_t *order,
+                             const float *As, int n_stages, int n_theta,
+                             const float *grad_out, const float *stage_points,
+                             int nstepsolver, int adaptive, float *moments,
+                             float *grad_points, cpab_stream_t stream);
+
+/*
  * Fused transform_data (2D/3D):
  *   out = interpolate(data, transform_grid(meshgrid, theta), out_size)
  * in one kernel, for n_theta transformations given by As/trels (as for

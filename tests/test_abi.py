@@ -110,6 +110,22 @@ def test_transform_data_entry_points_validate():
     assert fwd(2, NC2, sz, P, None, P, P, 0, 50, 0, P, 1, sz, P, P, None) == 0
 
 
+def test_chain_entry_points_validate():
+    L = _native.lib()
+    f, g = L.cpab_b200_forward_chain, L.cpab_b200_backward_chain
+    err = lambda: L.cpab_b200_last_error().decode()  # noqa: E731
+    nc1 = (ctypes.c_int32 * 1)(4)
+    assert f(1, nc1, P, 10, 0, None, P, P, 2, 1, 50, 0, P, P, None) == -1 and "ndim" in err()
+    assert f(2, NC2, P, 10, 0, None, P, P, 0, 1, 50, 0, P, P, None) == -1 and "n_stages" in err()
+    assert f(2, NC2, P, 10, 0, None, P, P, 3, 1, 50, 0, None, P, None) == -1
+    assert f(2, NC2, P, 10, 0, None, None, P, 3, 1, 50, 0, P, P, None) == -1 and "trels" in err()
+    assert f(2, NC2, P, 10, 0, None, P, P, 3, 1, 0, 0, P, P, None) == -2
+    assert g(2, NC2, P, 10, 0, None, P, 3, 1, P, P, 50, 0, None, None, None) == -1
+    assert "moments" in err()
+    assert g(2, NC2, P, 10, 0, None, P, 3, 1, P, None, 50, 0, P, None, None) == -1
+    assert f(2, NC2, P, 0, 0, None, P, P, 3, 1, 50, 0, P, P, None) == 0  # no points
+
+
 def test_errors_are_per_thread():
     import threading
     L = _native.lib()
