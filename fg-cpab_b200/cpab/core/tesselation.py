@@ -27,6 +27,8 @@ The full constraint matrix L is still available (``Tesselation.L``), built
 lazily on first access.
 """
 import os
+import uuid
+import warnings
 from itertools import combinations
 
 import numpy as np
@@ -96,13 +98,24 @@ class Tesselation:
         return False
 
     def _save_cache(self):
-        os.makedirs(self.dir, exist_ok=True)
+        """Write the basis next to the others.  Several processes (one per
+        GPU) may build the same basis at once on a fresh machine: each writes
+        its own temporary file and renames it atomically, so readers only ever
+        see a complete file, and a failed write only costs the cache."""
         stem = os.path.join(self.dir, self._stem())
         B = self.B.tocsr()
-        tmp = stem + ".tmp.npz"
-        np.savez(tmp, data=B.data, indices=B.indices, indptr=B.indptr,
-                 shape=np.asarray(B.shape), nodal_vertices=self.nodal_vertices)
-        os.replace(tmp, stem + ".npz")
+        tmp = "%s.%d.%s.tmp.npz" % (stem, os.getpid(), uuid.uuid4().hex[:8])
+        try:
+            os.makedirs(self.dir, exist_ok=True)
+            np.savez(tmp, data=B.data, indices=B.indices, indptr=B.indptr,
+                     shape=np.asarray(B.shape), nodal_vertices=self.nodal_vertices)
+            os.replace(tmp, stem + ".npz")
+        except OSError as e:
+            warnings.warn("could not cache the CPA basis in %s: %s" % (self.dir, e))
+            try:
+                os.remove(tmp)
+            except OSError:
+                pass
 
     # ------------------------------------------------------------ geometry
     def get_cell_centers(self):

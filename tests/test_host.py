@@ -1,5 +1,7 @@
 """Host-side logic that needs no GPU: the Cpab API surface, argument
 checks, grid layout, sharding."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -71,3 +73,33 @@ def test_shard_points_slices_last_axis():
     x = torch.arange(30.0).reshape(3, 10)
     parts = [shard_points(x, r, 3) for r in range(3)]
     assert torch.equal(torch.cat(parts, dim=1), x)
+
+
+def _build_basis_in(direc, out_q):
+    try:
+        import sys
+        sys.path[:0] = [os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                     "fg-cpab_b200")]
+        from cpab.core.tesselation import Tesselation2D
+        T = Tesselation2D([9, 7], [0, 0], [1, 1], direc=direc)
+        out_q.put(("ok", T.B.nnz))
+    except BaseException as e:  # reported to the parent
+        out_q.put(("error", repr(e)))
+
+
+def test_basis_cache_survives_concurrent_writers(tmp_path):
+    """One process per GPU builds the same basis on a fresh machine: all of
+    them must succeed and leave one complete cache file."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_build_basis_in, args=(str(tmp_path), q)) for _ in range(4)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[0] == "ok" for r in results), results
+    assert len({r[1] for r in results}) == 1
+    files = sorted(f.name for f in tmp_path.iterdir())
+    assert len(files) == 1 and files[0].endswith(".npz") and ".tmp" not in files[0]
