@@ -5,7 +5,9 @@ enqueued on torch's current stream of the tensors' device.  There is no CPU
 fallback: if the library is missing or the tensors are not CUDA tensors the
 call raises.
 """
+import contextlib
 import ctypes
+import functools
 import os
 
 import torch
@@ -96,12 +98,31 @@ def _require(t, name, dtype=torch.float32):
         raise RuntimeError("%s must be contiguous" % name)
 
 
+@functools.lru_cache(maxsize=256)
+def _i32_cached(values):
+    return (ctypes.c_int32 * len(values))(*values)
+
+
+@functools.lru_cache(maxsize=256)
+def _i64_cached(values):
+    return (ctypes.c_int64 * len(values))(*values)
+
+
 def _i32_array(values):
-    return (ctypes.c_int32 * len(values))(*[int(v) for v in values])
+    """Read-only int32 array for a call (tessellation sizes): cached per value."""
+    return _i32_cached(tuple(int(v) for v in values))
 
 
 def _i64_array(values):
-    return (ctypes.c_int64 * len(values))(*[int(v) for v in values])
+    """Read-only int64 array for a call (tensor sizes): cached per value."""
+    return _i64_cached(tuple(int(v) for v in values))
+
+
+def _on(device):
+    """Context making `device` current; nothing to do when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 # ---------------------------------------------------------------------------
@@ -113,7 +134,7 @@ def expm(As, dT):
     _require(As, "As")
     n, nd = As.shape[0], As.shape[1]
     out = torch.empty_like(As)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_expm(nd, _ptr(As), n, float(dT), _ptr(out), _stream(As.device)))
     return out
 
@@ -125,7 +146,7 @@ def build_A(ndim, nC, basis, theta, dT=None):
     n_theta = theta.shape[0]
     As = torch.empty((n_theta, nC, ndim, ndim + 1), device=theta.device, dtype=torch.float32)
     trels = torch.empty_like(As) if dT is not None else None
-    with torch.cuda.device(theta.device):
+    with _on(theta.device):
         _check(lib().cpab_b200_build_A(
             ndim, nC, basis.d, n_theta, _ptr(basis.rowptr), _ptr(basis.colidx), _ptr(basis.vals),
             _ptr(theta), float(dT) if dT is not None else 0.0, _ptr(As), _ptr(trels),
@@ -142,7 +163,7 @@ def order_points(nc, points, batched):
     nC = int(np_prod(nc)) * {1: 1, 2: 4, 3: 5}[nd]
     counts = torch.empty((n_sets, nC), device=points.device, dtype=torch.int32)
     order = torch.empty((n_sets, nP), device=points.device, dtype=torch.int32)
-    with torch.cuda.device(points.device):
+    with _on(points.device):
         _check(lib().cpab_b200_order_points(nd, _i32_array(nc), _ptr(points), nP, n_sets,
                                             _ptr(counts), _ptr(order), _stream(points.device)))
     return order
@@ -161,7 +182,7 @@ def forward(ndim, nc, points, batched, trels, As, nstepsolver, adaptive, order=N
     n_theta = As.shape[0]
     nP = points.shape[-1]
     out = torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         if ndim == 1:
             _check(lib().cpab_b200_forward_1d_closed_form(
                 _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_theta, int(nc[0]),
@@ -187,7 +208,7 @@ def backward(ndim, nc, points, batched, As, grad_out, nstepsolver, adaptive, wan
     moments = torch.empty((n_theta, nC, ppc), device=As.device, dtype=torch.float32)
     gp = (torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
           if want_points else None)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_backward(
             ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_theta,
             _ptr(grad_out), int(nstepsolver), int(adaptive), _ptr(moments), _ptr(gp),
@@ -200,7 +221,7 @@ def cell_index(nc, points):
     _require(points, "points")
     nd, n = points.shape
     out = torch.empty(n, device=points.device, dtype=torch.int32)
-    with torch.cuda.device(points.device):
+    with _on(points.device):
         _check(lib().cpab_b200_cell_index(nd, _i32_array(nc), _ptr(points), n, _ptr(out),
                                           _stream(points.device)))
     return out
@@ -212,7 +233,7 @@ def project(basis, moments):
     n_theta = moments.shape[0]
     D = moments[0].numel()
     out = torch.empty((n_theta, basis.d), device=moments.device, dtype=torch.float32)
-    with torch.cuda.device(moments.device):
+    with _on(moments.device):
         _check(lib().cpab_b200_project(
             basis.d, D, n_theta, _ptr(basis.t_rowptr), _ptr(basis.t_colidx), _ptr(basis.t_vals),
             _ptr(moments), _ptr(out), _stream(moments.device)))
@@ -224,7 +245,7 @@ def interpolate(ndim, data, grid, outsize):
     _require(grid, "grid")
     B, C = data.shape[0], data.shape[1]
     out = torch.empty((B, C, *outsize), device=data.device, dtype=torch.float32)
-    with torch.cuda.device(data.device):
+    with _on(data.device):
         _check(lib().cpab_b200_interpolate(
             ndim, _ptr(data), B, C, _i64_array(data.shape[2:]), _ptr(grid), _i64_array(outsize),
             _ptr(out), _stream(data.device)))
@@ -238,7 +259,7 @@ def interpolate_backward(ndim, data, grid, outsize, grad_out, want_grid, want_da
     B, C = data.shape[0], data.shape[1]
     gg = torch.empty_like(grid) if want_grid else None
     gd = torch.empty_like(data) if want_data else None
-    with torch.cuda.device(data.device):
+    with _on(data.device):
         _check(lib().cpab_b200_interpolate_backward(
             ndim, _ptr(data), B, C, _i64_array(data.shape[2:]), _ptr(grid), _i64_array(outsize),
             _ptr(grad_out), _ptr(gg), _ptr(gd), _stream(data.device)))
@@ -256,7 +277,7 @@ def transform_data(ndim, nc, outsize, axes, trels, As, nstepsolver, adaptive, da
     P = int(np_prod(outsize))
     out = torch.empty((n_theta, C, *outsize), device=As.device, dtype=torch.float32)
     grid_t = torch.empty((n_theta, ndim, P), device=As.device, dtype=torch.float32)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_transform_data(
             ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(trels),
             _ptr(As), n_theta,
@@ -275,7 +296,7 @@ def transform_data_backward(ndim, nc, outsize, axes, As, nstepsolver, adaptive, 
     n_theta, nC, C = As.shape[0], As.shape[1], data.shape[1]
     moments = torch.empty((n_theta, nC, ndim * (ndim + 1)), device=As.device, dtype=torch.float32)
     gd = torch.empty_like(data) if want_data else None
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_transform_data_backward(
             ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(As), n_theta,
             int(nstepsolver), int(adaptive), _ptr(data), C, _i64_array(data.shape[2:]),
@@ -295,7 +316,7 @@ def forward_chain(ndim, nc, points, batched, trels, As, n_stages, nstepsolver, a
     out = torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
     sp = (torch.empty((n_stages - 1, n_theta, ndim, nP), device=As.device, dtype=torch.float32)
           if n_stages > 1 else None)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_forward_chain(
             ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(trels),
             _ptr(As), n_stages, n_theta, int(nstepsolver), int(adaptive), _ptr(sp), _ptr(out),
@@ -315,7 +336,7 @@ def backward_chain(ndim, nc, points, batched, As, n_stages, grad_out, stage_poin
                           dtype=torch.float32)
     gp = (torch.empty((n_theta, ndim, nP), device=As.device, dtype=torch.float32)
           if want_points else None)
-    with torch.cuda.device(As.device):
+    with _on(As.device):
         _check(lib().cpab_b200_backward_chain(
             ndim, _i32_array(nc), _ptr(points), nP, int(batched), _ptr(order), _ptr(As), n_stages,
             n_theta, _ptr(grad_out), _ptr(stage_points), int(nstepsolver), int(adaptive),
