@@ -2,7 +2,8 @@
 
     python tests/golden/make_golden.py [path/to/reference]
 
-Needs the reference source tree (default /root/reference); it is copied to a
+Needs the reference source tree (the path argument; its default is the checkout
+location this build used); it is copied to a
 temporary directory first because constructing a reference tessellation writes
 a basis cache next to the package.  The reference's cpab/__init__.py
 JIT-compiles CUDA, so cpab.core and cpab.pytorch.interpolation are loaded as
