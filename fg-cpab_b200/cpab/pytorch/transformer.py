@@ -110,7 +110,10 @@ def _order(params, points, batched):
     permutation of the right size.
     """
     nP = points.shape[-1]
-    if nP < ORDER_MIN_POINTS:
+    # 1D: few cells, so a sorted warp would funnel all its lanes into the same
+    # shared-memory moment counters (compare-and-swap retries); storage order
+    # measured 17% faster per step there.
+    if nP < ORDER_MIN_POINTS or params.ndim == 1:
         return None
     cache = params.__dict__.setdefault("_order_cache", {})
     key = (points.data_ptr(), points._version, tuple(points.shape), bool(batched),
