@@ -267,15 +267,15 @@ __device__ __forceinline__ void affine(const float (&m)[Dim<ND>::kPpc], const fl
     const float2 r = __ffma2_rn(c0, bc(p[0]), __ffma2_rn(c1, bc(p[1]), c2));
     v[0] = r.x;
     v[1] = r.y;
-    return;
-  }
+  } else {
 #pragma unroll
-  for (int r = 0; r < ND; ++r) {
-    const float *row = m + r * (ND + 1);
-    float acc = row[ND];
+    for (int r = 0; r < ND; ++r) {
+      const float *row = m + r * (ND + 1);
+      float acc = row[ND];
 #pragma unroll
-    for (int k = ND - 1; k >= 0; --k) acc = __fmaf_rn(row[k], p[k], acc);
-    v[r] = acc;
+      for (int k = ND - 1; k >= 0; --k) acc = __fmaf_rn(row[k], p[k], acc);
+      v[r] = acc;
+    }
   }
 }
 

@@ -281,7 +281,9 @@ __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &
     const int64_t off = ((int64_t)st * a.n_theta + b) * a.nC * P;
     const float *tab = SMEM ? s_tab : a.trels + off;
     const float *ag = a.As + off;
-#pragma unroll 2
+    // Unrolled by a divisor of the usual T = 50 (loop control is ~4% of a step);
+    // measured: 2D 139 -> 136 us, 3D 971 -> 940 us on the bench shapes.
+#pragma unroll(ND == 3 ? 10 : 5)
     for (int n = 0; n < T; ++n) {
       const int c = lookup<ND>(t, p);
       float m[P];
