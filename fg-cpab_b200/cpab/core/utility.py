@@ -80,3 +80,8 @@ def null(A, eps=1e-6, zero_tol=None):
     Z = sp.csr_matrix(Z)
     Z.eliminate_zeros()
     return Z
+
+
+def make_hashable(arr):
+    """Rows of a 2D array as a tuple of tuples (usable in sets and as keys)."""
+    return tuple(tuple(row.tolist()) for row in arr)

@@ -57,6 +57,27 @@ def device_basis(params, device):
     return hit
 
 
+def _get_sparse_basis(params, device, dtype=torch.float32):
+    """B as a coalesced torch sparse COO tensor on `device` (the helper of the
+    reference's transformer module, cpab/pytorch/transformer.py:47-66, kept for
+    code that uses it; the kernels here read the CSR copy of device_basis).
+    Like the reference, the cuda:0 float32 copy is kept in
+    params.basis_gpu_sparse and its transpose in params.basis_gpu_sparse_t."""
+    device = torch.device(device)
+    cached = getattr(params, "basis_gpu_sparse", None)
+    if cached is not None and cached.device == device and cached.dtype == dtype:
+        return cached
+    coo = params.basis.tocoo()
+    idx = torch.stack((torch.from_numpy(coo.row.astype(np.int64)),
+                       torch.from_numpy(coo.col.astype(np.int64)))).to(device)
+    B = torch.sparse_coo_tensor(idx, torch.from_numpy(coo.data).to(device=device, dtype=dtype),
+                                size=params.basis.shape, device=device, dtype=dtype).coalesce()
+    if device.type == "cuda" and device.index in (None, 0) and dtype == torch.float32:
+        params.basis_gpu_sparse = B
+        params.basis_gpu_sparse_t = B.transpose(0, 1).coalesce()
+    return B
+
+
 def CPAB_transformer(points, theta, params, compute_points_grad=False):
     """Transform points through the CPA velocity field given by theta.
 

@@ -103,3 +103,14 @@ def test_basis_cache_survives_concurrent_writers(tmp_path):
     assert len({r[1] for r in results}) == 1
     files = sorted(f.name for f in tmp_path.iterdir())
     assert len(files) == 1 and files[0].endswith(".npz") and ".tmp" not in files[0]
+
+
+def test_reference_helpers_exist():
+    """Helpers of the reference's modules that user code may import."""
+    from cpab.core.utility import make_hashable
+    from cpab.pytorch.transformer import _get_sparse_basis
+    assert make_hashable(np.array([[1, 2], [3, 4]])) == ((1, 2), (3, 4))
+    C = Cpab([3, 3], zero_boundary=True)
+    B = _get_sparse_basis(C.params, "cpu", torch.float64)
+    assert B.is_sparse and tuple(B.shape) == C.params.basis.shape
+    np.testing.assert_allclose(B.to_dense().numpy(), C.params.basis.toarray())
