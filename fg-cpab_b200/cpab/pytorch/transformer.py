@@ -71,7 +71,8 @@ def _get_sparse_basis(params, device, dtype=torch.float32):
     idx = torch.stack((torch.from_numpy(coo.row.astype(np.int64)),
                        torch.from_numpy(coo.col.astype(np.int64)))).to(device)
     B = torch.sparse_coo_tensor(idx, torch.from_numpy(coo.data).to(device=device, dtype=dtype),
-                                size=params.basis.shape, device=device, dtype=dtype).coalesce()
+                                size=params.basis.shape, device=device, dtype=dtype,
+                                check_invariants=False).coalesce()  # indices from a valid COO
     if device.type == "cuda" and device.index in (None, 0) and dtype == torch.float32:
         params.basis_gpu_sparse = B
         params.basis_gpu_sparse_t = B.transpose(0, 1).coalesce()
