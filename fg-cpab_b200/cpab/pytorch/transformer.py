@@ -72,7 +72,7 @@ def _get_sparse_basis(params, device, dtype=torch.float32):
                        torch.from_numpy(coo.col.astype(np.int64)))).to(device)
     B = torch.sparse_coo_tensor(idx, torch.from_numpy(coo.data).to(device=device, dtype=dtype),
                                 size=params.basis.shape, device=device, dtype=dtype,
-                                check_invariants=False).coalesce()  # indices from a valid COO
+                                check_invariants=True).coalesce()  # O(nnz), once per device
     if device.type == "cuda" and device.index in (None, 0) and dtype == torch.float32:
         params.basis_gpu_sparse = B
         params.basis_gpu_sparse_t = B.transpose(0, 1).coalesce()
