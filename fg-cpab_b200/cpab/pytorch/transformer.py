@@ -70,9 +70,9 @@ def _get_sparse_basis(params, device, dtype=torch.float32):
     coo = params.basis.tocoo()
     idx = torch.stack((torch.from_numpy(coo.row.astype(np.int64)),
                        torch.from_numpy(coo.col.astype(np.int64)))).to(device)
-    B = torch.sparse_coo_tensor(idx, torch.from_numpy(coo.data).to(device=device, dtype=dtype),
-                                size=params.basis.shape, device=device, dtype=dtype,
-                                check_invariants=True).coalesce()  # O(nnz), once per device
+    with torch.sparse.check_sparse_tensor_invariants(enable=True):  # O(nnz), once per device
+        B = torch.sparse_coo_tensor(idx, torch.from_numpy(coo.data).to(device=device, dtype=dtype),
+                                    size=params.basis.shape, device=device, dtype=dtype).coalesce()
     if device.type == "cuda" and device.index in (None, 0) and dtype == torch.float32:
         params.basis_gpu_sparse = B
         params.basis_gpu_sparse_t = B.transpose(0, 1).coalesce()
