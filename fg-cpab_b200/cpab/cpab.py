@@ -77,7 +77,8 @@ class Cpab(object):
         coo = self.params.basis.tocoo()
         idx = torch.from_numpy(np.vstack((coo.row, coo.col)).astype(np.int64)).to(device)
         val = torch.from_numpy(coo.data).to(device=device, dtype=dtype)
-        return torch.sparse_coo_tensor(idx, val, size=self.params.basis.shape).coalesce()
+        with torch.sparse.check_sparse_tensor_invariants(enable=True):
+            return torch.sparse_coo_tensor(idx, val, size=self.params.basis.shape).coalesce()
 
     def set_solver_params(self, nstepsolver=50, adaptive_substeps=False):
         """Set parameters controlling the integration algorithm.
