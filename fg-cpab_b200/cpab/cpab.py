@@ -119,30 +119,41 @@ class Cpab(object):
         K[(i,p),(j,q)] = v^2 exp(-M/(2 l^2)) with M = |c_i - c_j|^2 when p == q
         and M = 100 max|c_i - c_j|^2 otherwise (c = cell centres).
         """
+        cov = self._prior_covariance(length_scale, output_variance)
+        return self.sample_transformation(n_sample, mean=mean, cov=cov)
+
+    def _prior_covariance(self, length_scale=0.1, output_variance=1, device=None):
+        """[d, d] covariance of sample_transformation_with_prior: B^T K B, with
+        K split per cell parameter k as E (nC x nC, same parameter) plus a
+        constant for all other entries, so that only nC x nC and d x d
+        matrices are formed (the reference builds K as a dense D x D matrix in a
+        loop over cell pairs)."""
         p = self.params
+        device = _DEVICE if device is None else device
         ppc = p.params_pr_cell
         centers = torch.tensor(self.tesselation.get_cell_centers(), dtype=torch.float32,
-                               device=_DEVICE)
+                               device=device)
         sq = (centers * centers).sum(1, keepdim=True)
         dist = sq - 2 * centers @ centers.t() + sq.t()
         scale = 2 * length_scale ** 2
         var = output_variance ** 2
         E = var * torch.exp(-(dist / scale))                    # same-parameter blocks
         e_off = var * torch.exp(-(100 * dist.max()) / scale)    # cross-parameter entries
-        cov = torch.zeros(p.d, p.d, device=_DEVICE)
-        s = torch.zeros(p.d, device=_DEVICE)
+        cov = torch.zeros(p.d, p.d, device=device)
+        s = torch.zeros(p.d, device=device)
         basis = p.basis.tocsr()
         for k in range(ppc):
             Bk = basis[k::ppc].tocoo()                           # parameter k of every cell, [nC, d]
-            idx = torch.from_numpy(np.vstack((Bk.col, Bk.row)).astype(np.int64)).to(_DEVICE)
-            BkT = torch.sparse_coo_tensor(idx, torch.from_numpy(Bk.data).float().to(_DEVICE),
-                                          size=(p.d, p.nC)).coalesce()
+            idx = torch.from_numpy(np.vstack((Bk.col, Bk.row)).astype(np.int64)).to(device)
+            with torch.sparse.check_sparse_tensor_invariants(enable=True):
+                BkT = torch.sparse_coo_tensor(idx, torch.from_numpy(Bk.data).float().to(device),
+                                              size=(p.d, p.nC)).coalesce()
             EBk = torch.sparse.mm(BkT, E).t()                    # E Bk (E symmetric), [nC, d]
             sk = torch.sparse.sum(BkT, dim=1).to_dense()
             cov += torch.sparse.mm(BkT, EBk) - e_off * torch.outer(sk, sk)
             s += sk
         cov += e_off * torch.outer(s, s)
-        return self.sample_transformation(n_sample, mean=mean, cov=cov)
+        return cov
 
     def identity(self, n_sample=1, epsilon=0):
         """[n_sample, d] identity parameters (zeros), plus epsilon."""

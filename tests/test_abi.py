@@ -13,7 +13,8 @@ HEADER = os.path.join(ROOT, "include", "cpab_b200.h")
 
 
 def declared():
-    text = open(HEADER).read()
+    with open(HEADER) as f:
+        text = f.read()
     return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(cpab_b200_\w+)\s*\(", text, re.M)))
 
 

@@ -155,3 +155,17 @@ def test_order_cache_reuses_and_invalidates():
     # and an order for the right points is a permutation
     assert torch.equal(torch.sort(o3.flatten())[0], torch.arange(20000, device=DEV, dtype=torch.int32))
     assert tr.ORDER_MIN_POINTS <= 20000
+
+
+def test_sample_transformation_with_prior_on_gpu():
+    """Samples of the smooth prior: right shape, and their empirical covariance
+    follows the prior's (checked on the largest-variance directions)."""
+    C = cpab((4, 4))
+    torch.manual_seed(3)
+    th = C.sample_transformation_with_prior(20000, length_scale=0.2, output_variance=1.0)
+    assert th.shape == (20000, C.params.d) and th.is_cuda and torch.isfinite(th).all()
+    cov = C._prior_covariance(0.2, 1.0).double()
+    emp = torch.cov(th.double().t())
+    top = torch.argsort(torch.diagonal(cov), descending=True)[:20]
+    rel = (torch.diagonal(emp)[top] - torch.diagonal(cov)[top]).abs() / torch.diagonal(cov)[top]
+    assert float(rel.max()) < 0.1   # 20000 samples: ~1% standard error per variance

@@ -114,3 +114,26 @@ def test_reference_helpers_exist():
     B = _get_sparse_basis(C.params, "cpu", torch.float64)
     assert B.is_sparse and tuple(B.shape) == C.params.basis.shape
     np.testing.assert_allclose(B.to_dense().numpy(), C.params.basis.toarray())
+
+
+@pytest.mark.parametrize("tess,zb", [([5], True), ([3, 3], True), ([3, 2], False), ([2, 2, 2], True)])
+def test_prior_covariance_equals_the_dense_construction(tess, zb):
+    """sample_transformation_with_prior's covariance B^T K B against K built as
+    the reference does: a dense D x D matrix, entry ((i,p),(j,q)) =
+    v^2 exp(-M/(2 l^2)), M = |c_i - c_j|^2 when p == q, else 100 max |c_i - c_j|^2."""
+    C = Cpab(tess, zero_boundary=zb)
+    l, v = 0.15, 1.3
+    cov = C._prior_covariance(l, v, device="cpu").double()
+    ppc, nC = C.params.params_pr_cell, C.params.nC
+    c = torch.tensor(C.tesselation.get_cell_centers(), dtype=torch.float32)
+    norm = (c * c).sum(1, keepdim=True)
+    dist = norm - 2 * c @ c.t() + norm.t()
+    M = torch.full((nC * ppc, nC * ppc), float(100 * dist.max()))
+    for k in range(ppc):
+        M[k::ppc, k::ppc] = dist
+    K = (v ** 2 * torch.exp(-(M / (2 * l ** 2)))).double()
+    B = torch.from_numpy(C.params.basis.toarray()).double()
+    ref = B.t() @ K @ B
+    tol = 1e-5 * float(ref.abs().max())
+    assert float((cov - ref).abs().max()) <= tol
+    assert torch.allclose(cov, cov.t(), atol=tol)
