@@ -156,15 +156,9 @@ static __device__ __noinline__ int cell_of_3d_outside(int nx, int ny, int nz, fl
                      fminf(fmaxf(py, 0.0f), 1.0f) * fy, fminf(fmaxf(pz, 0.0f), 1.0f) * fz);
 }
 
-// Tetrahedron of a point with 0 <= s* < n* (cube coordinates): no clamping.
-__device__ __forceinline__ int tet_in_cube_inside(int nx, int ny, float sx, float sy, float sz) {
-  int i, j, k;
-  const float fi = floor_nonneg(sx, i);
-  const float fj = floor_nonneg(sy, j);
-  const float fk = floor_nonneg(sz, k);
-  float x = sx - fi;
-  float y = sy - fj;
-  const float z = sz - fk;
+// Tetrahedron of cube (i, j, k) holding local coordinates (x, y, z) in [0, 1).
+__device__ __forceinline__ int tet_from_local(int nx, int ny, int i, int j, int k, float x,
+                                              float y, float z) {
   const int c = 5 * (i + nx * (j + ny * k));
   if ((i ^ j ^ k) & 1) {
     const float x0 = x;
@@ -182,8 +176,19 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float 
   // In [0, 1) the reference's clamps are identities, the corner rule does not
   // apply, and p * n rounds below n, so floor(p * n) <= n - 1 needs no clamp;
   // everything else (including coordinates exactly 1) takes the general path.
-  if (px >= 0.0f && px < 1.0f && py >= 0.0f && py < 1.0f && pz >= 0.0f && pz < 1.0f)
-    return tet_in_cube_inside(t.nx, t.ny, px * t.fx, py * t.fy, pz * t.fz);
+  if (px >= 0.0f && px < 1.0f && py >= 0.0f && py < 1.0f && pz >= 0.0f && pz < 1.0f) {
+    // floor_nonneg of x and y together (paired instructions, same roundings):
+    // r = 2^23 + floor(s), floor = r - 2^23, and s - floor is exact.
+    const float2 sxy = __fmul2_rn(make_float2(px, py), make_float2(t.fx, t.fy));
+    const float2 r = __fadd2_rd(sxy, make_float2(8388608.0f, 8388608.0f));
+    const float2 fxy = __fadd2_rn(r, make_float2(-8388608.0f, -8388608.0f));
+    const float2 lxy = __ffma2_rn(fxy, make_float2(-1.0f, -1.0f), sxy);
+    int k;
+    const float sz = pz * t.fz;
+    const float fk = floor_nonneg(sz, k);
+    return tet_from_local(t.nx, t.ny, __float_as_int(r.x) - 0x4B000000,
+                          __float_as_int(r.y) - 0x4B000000, k, lxy.x, lxy.y, sz - fk);
+  }
   return cell_of_3d_outside(t.nx, t.ny, t.nz, px, py, pz);
 }
 
