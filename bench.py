@@ -68,6 +68,11 @@ def profiled(key):
     return None
 
 
+ORDER_NOTE = "points sorted by cell inside every timed step (no order kept across steps)"
+MESH_ORDER_NOTE = ("meshgrid points generated in the kernels; 3D visits them in a cell order "
+                   "that depends only on the tessellation and output size, computed once")
+
+
 def config(world):
     return {
         "workload": "2D Cpab([20,20], zero_boundary=True): batch 16, 125,000 U[0,1]^2 points per "
@@ -77,63 +82,78 @@ def config(world):
         "global_batch": BATCH * N_POINTS * world,
         "parallelism": "points sharded over %d GPU(s), dtheta allreduce" % world,
         "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20),
+        "point_order": ORDER_NOTE,
     }
+
+
+_SAMPLER = r"""
+import json, select, sys
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+out = {"max": pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), "s": []}
+def sample():
+    try:
+        out["s"].append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                         int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
+    except Exception:
+        pass
+sample()
+print("ready", flush=True)
+while not select.select([sys.stdin], [], [], 0.001)[0]:
+    sample()
+sample()
+print(json.dumps(out), flush=True)
+"""
 
 
 class Clocks:
     """SM clock and throttle-reason samples (NVML, every millisecond, plus one
-    when sampling stops) taken in a background thread while the timed region
-    runs; the timed region of a default run lasts only ~12 ms."""
+    when sampling stops) taken while the timed region runs; the timed region
+    of a default run lasts only ~12 ms.  The sampler is a child process, so
+    that it takes no time from this process's Python thread (the 1D step is
+    bound by host time)."""
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.samples = []
-        self.stop_flag = None
-        self.thread = None
+        self.proc = None
 
     def start(self):
-        import threading
+        import subprocess
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index)],
+                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            if self.proc.stdout.readline().strip() != "ready":
+                raise RuntimeError("clock sampler did not start")
         except Exception:
-            return
-        self.stop_flag = threading.Event()
-
-        def sample():
-            try:
-                self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
-                                     pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
-            except Exception:
-                pass
-
-        def run():
-            while not self.stop_flag.is_set():
-                sample()
-                self.stop_flag.wait(0.001)
-            sample()
-
-        self.thread = threading.Thread(target=run, daemon=True)
-        self.thread.start()
+            if self.proc is not None:
+                self.proc.kill()
+                self.proc.wait()
+            self.proc = None
 
     def stop(self):
-        if self.thread is None:
+        if self.proc is None:
             return None
-        self.stop_flag.set()
-        self.thread.join()
-        if not self.samples:
+        try:
+            out, _ = self.proc.communicate("stop\n", timeout=30)
+            d = json.loads(out.strip().splitlines()[-1])
+        except Exception:
+            self.proc.kill()
+            self.proc.wait()
+            return None
+        samples = d["s"]
+        if not samples:
             return None
         mask = 0
-        for _, r in self.samples:
+        for _, r in samples:
             mask |= int(r)
-        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
-                "sm_max_mhz": self.max_mhz,
+        return {"sm_mhz": statistics.median(m for m, _ in samples),
+                "sm_max_mhz": d["max"],
                 "reasons": sorted(n for n, bit in self.REASONS.items() if mask & bit),
-                "samples": len(self.samples)}
+                "samples": len(samples)}
 
 
 def init_dist():
@@ -344,6 +364,43 @@ def blobs(shape, g, n=20):
     return vol
 
 
+def graph_replay(step, resident, C, flush, steps, warmup):
+    """ms per replay of the device-resident step captured in one CUDA graph."""
+    from cpab.pytorch.transformer import clear_order_cache
+
+    theta = resident["theta"].detach().clone().requires_grad_(True)
+    static = dict(resident, theta=theta)
+
+    def call():
+        clear_order_cache(C.params)   # the sort is recorded into the graph
+        theta.grad = None
+        return step(static)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        call()
+    for _ in range(max(warmup, 1)):
+        g.replay()
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        ev.append((s, e))
+    torch.cuda.synchronize()
+    del g
+    return sum(s.elapsed_time(e) for s, e in ev) / steps
+
+
 def run_ours(args, rank, world, local):
     from cpab import _native
 
@@ -362,6 +419,8 @@ def run_ours(args, rank, world, local):
 
     def timed(name):
         def call(*a, **k):
+            if timings.get("capture"):  # no timing events inside a CUDA graph capture
+                return orig[name](*a, **k)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             r = orig[name](*a, **k)
@@ -396,7 +455,12 @@ def run_ours(args, rank, world, local):
     resident = {k: v.to(dev) for k, v in host.items()}
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
 
+    from cpab.pytorch.transformer import clear_order_cache
+
     def dev_step():
+        # Every step sorts its points again, as a step on a new batch would
+        # (the library would otherwise keep the order of the unchanged points).
+        clear_order_cache(C.params)
         return step(dict(resident, theta=resident["theta"].detach()))
 
     for _ in range(args.warmup):
@@ -462,6 +526,15 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.barrier()
     e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world) / args.steps
+
+    # One GPU: the same device-resident step captured once in a CUDA graph
+    # (sort, forward, loss, backward, projection recorded; every replay runs
+    # them all), which removes the host launch gaps between its kernels.
+    graph_ms = None
+    if world == 1 and not args.no_graph:
+        timings["capture"] = True
+        graph_ms = graph_replay(step, resident, C, flush, args.steps, args.warmup)
+        timings["capture"] = False
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = 4 + host["theta"].numel() * 4
 
@@ -504,7 +577,8 @@ def run_ours(args, rank, world, local):
         cfg = config(world) if default else {
             "workload": w.desc, "tess": w.tess, "batch": w.batch, "stages": w.stages,
             "nstepsolver": NSTEP, "global_batch": pairs_step, "parallelism": w.parallelism,
-            "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20)}
+            "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20),
+            "point_order": MESH_ORDER_NOTE if fused else ORDER_NOTE}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -521,6 +595,10 @@ def run_ours(args, rank, world, local):
                          "algorithmic_bytes_per_launch": bwd_bytes},
             "issue_roofline": issue,
             "kernel_ms": kern,
+            "graph_replay": None if graph_ms is None else {
+                "value": pairs_step / (graph_ms * 1e-3), "unit": UNIT, "ms_per_step": graph_ms,
+                "note": "the value step captured once in a CUDA graph and replayed; "
+                        "value and e2e above are eager"},
             "gpu_launches": counted["n"],
             "clocks": clk,
         }
@@ -552,6 +630,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="skip the one-GPU CUDA graph replay measurement")
     ap.add_argument("--config", default="2d",
                     choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d"],
                     help="workload (default: BASELINE configs[1], 2D 20x20)")

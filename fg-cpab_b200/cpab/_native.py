@@ -82,11 +82,21 @@ def _check(status):
 
 
 def _ptr(t):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+    """Device pointer of t (None = NULL); ctypes converts it for the void* arguments."""
+    return t.data_ptr() if t is not None else None
+
+
+# The raw cudaStream_t of the current stream in one call (torch's own query for
+# generated kernels); current_stream() builds a Stream object per call, which
+# is a sizeable share of a call's host time.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def _stream(device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def _require(t, name, dtype=torch.float32):

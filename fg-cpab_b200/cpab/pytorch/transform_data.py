@@ -26,12 +26,14 @@ def _mesh(params, outsize, device):
     starts inside one tetrahedron loads its rows once (the unsorted output
     order crosses several cubes per warp and measured ~30% slower).  2D
     tables are staged in shared memory and output order (coalesced writes)
-    is used.
+    is used.  A miss under CUDA graph capture is built inside the graph and
+    not cached (its contents exist only in the graph's replays).
     """
     cache = params.__dict__.setdefault("_mesh_axes", {})
     key = (tuple(int(s) for s in outsize), str(device))
     hit = cache.get(key)
     if hit is None:
+        capturing = torch.cuda.is_current_stream_capturing()
         lin = [torch.linspace(params.domain_min[i], params.domain_max[i], int(n), device=device)
                for i, n in enumerate(outsize)]
         axes = torch.cat(lin).contiguous()
@@ -41,7 +43,8 @@ def _mesh(params, outsize, device):
             pts = torch.stack([g.reshape(-1) for g in mesh]).contiguous()
             order = _native.order_points(_nc(params), pts, False)[0].contiguous()
         hit = (axes, order)
-        cache[key] = hit
+        if not capturing:
+            cache[key] = hit
     return hit
 
 

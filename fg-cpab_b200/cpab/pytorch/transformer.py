@@ -130,6 +130,11 @@ def _order(params, points, batched):
     and shape.  A stale hit (a new tensor at a reused address) is harmless:
     results never depend on the processing order, which is always a
     permutation of the right size.
+
+    Under CUDA graph capture the sort is always recorded into the graph (a
+    replay may see new point values in the same buffer) and nothing is
+    cached: captured kernels have not run yet, so the order's contents are
+    only defined inside the graph's replays.
     """
     nP = points.shape[-1]
     # 1D: few cells, so a sorted warp would funnel all its lanes into the same
@@ -137,6 +142,8 @@ def _order(params, points, batched):
     # measured 17% faster per step there.
     if nP < ORDER_MIN_POINTS or params.ndim == 1:
         return None
+    if torch.cuda.is_current_stream_capturing():
+        return _native.order_points(_nc(params), points, batched)
     cache = params.__dict__.setdefault("_order_cache", {})
     key = (points.data_ptr(), points._version, tuple(points.shape), bool(batched),
            tuple(_nc(params)))
@@ -146,6 +153,11 @@ def _order(params, points, batched):
     order = _native.order_points(_nc(params), points, batched)
     cache[points.device] = (key, order)
     return order
+
+
+def clear_order_cache(params):
+    """Forget the kept point orders, so that the next call sorts its points again."""
+    params.__dict__.pop("_order_cache", None)
 
 
 class _CPABFunction(torch.autograd.Function):

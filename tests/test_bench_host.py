@@ -1,0 +1,50 @@
+"""Host-side pieces of bench.py that need no GPU: the clock sampler (a child
+process reading NVML, here a fake NVML module) and the config record."""
+import os
+import sys
+import time
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+FAKE_NVML = """
+NVML_CLOCK_SM = 1
+def nvmlInit(): pass
+def nvmlDeviceGetHandleByIndex(i): return i
+def nvmlDeviceGetMaxClockInfo(h, k): return 1965
+def nvmlDeviceGetClockInfo(h, k): return 1800
+def nvmlDeviceGetCurrentClocksEventReasons(h): return 0x4 | 0x40
+"""
+
+
+def test_clock_sampler_child_process(tmp_path, monkeypatch):
+    (tmp_path / "pynvml.py").write_text(FAKE_NVML)
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    c = bench.Clocks(0)
+    c.start()
+    assert c.proc is not None
+    time.sleep(0.05)
+    r = c.stop()
+    assert r["sm_mhz"] == 1800 and r["sm_max_mhz"] == 1965
+    assert r["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
+    assert r["samples"] >= 2
+    assert c.proc.returncode == 0
+
+
+def test_clock_sampler_without_nvml_reports_nothing(tmp_path, monkeypatch):
+    (tmp_path / "pynvml.py").write_text("raise ImportError('no NVML here')\n")
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    c = bench.Clocks(0)
+    c.start()
+    assert c.proc is None and c.stop() is None
+
+
+@pytest.mark.parametrize("world", [1, 8])
+def test_default_config_record(world):
+    cfg = bench.config(world)
+    assert cfg["global_batch"] == bench.BATCH * bench.N_POINTS * world
+    assert cfg["point_order"] == bench.ORDER_NOTE
+    assert "flushed" in cfg["l2"]
