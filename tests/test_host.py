@@ -137,3 +137,32 @@ def test_prior_covariance_equals_the_dense_construction(tess, zb):
     tol = 1e-5 * float(ref.abs().max())
     assert float((cov - ref).abs().max()) <= tol
     assert torch.allclose(cov, cov.t(), atol=tol)
+
+
+def test_order_cache_is_bypassed_under_graph_capture(monkeypatch):
+    """Inside a CUDA graph capture the point sort is recorded every call and
+    nothing is cached (captured buffers hold no data until a replay); outside
+    it the order of an unchanged points tensor is kept until cleared."""
+    from cpab import _native
+    from cpab.pytorch import transformer as tr
+
+    calls = []
+
+    def fake_order(nc, points, batched):
+        calls.append(points.data_ptr())
+        return torch.arange(points.shape[-1], dtype=torch.int32)[None]
+
+    C = Cpab([4, 4])
+    pts = torch.rand(2, 5000)
+    monkeypatch.setattr(_native, "order_points", fake_order)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    tr.clear_order_cache(C.params)
+    tr._order(C.params, pts, False)
+    tr._order(C.params, pts, False)
+    assert len(calls) == 2 and "_order_cache" not in C.params.__dict__
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    o1 = tr._order(C.params, pts, False)
+    assert tr._order(C.params, pts, False) is o1 and len(calls) == 3
+    tr.clear_order_cache(C.params)
+    tr._order(C.params, pts, False)
+    assert len(calls) == 4
