@@ -86,8 +86,11 @@ def config(world):
     }
 
 
+# NVML sampling period.
+CLOCK_INTERVAL_S = 0.002
+
 _SAMPLER = r"""
-import json, select, sys
+import json, os, select, sys
 import pynvml
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
@@ -98,9 +101,11 @@ def sample():
                          int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
     except Exception:
         pass
+print("idle", flush=True)
+os.read(0, 1)                      # "g": the timed region starts
 sample()
 print("ready", flush=True)
-while not select.select([sys.stdin], [], [], 0.001)[0]:
+while not select.select([0], [], [], float(sys.argv[2]))[0]:
     sample()
 sample()
 print(json.dumps(out), flush=True)
@@ -108,41 +113,54 @@ print(json.dumps(out), flush=True)
 
 
 class Clocks:
-    """SM clock and throttle-reason samples (NVML, every millisecond, plus one
-    when sampling stops) taken while the timed region runs; the timed region
-    of a default run lasts only ~12 ms.  The sampler is a child process, so
-    that it takes no time from this process's Python thread (the 1D step is
-    bound by host time)."""
+    """SM clock and throttle-reason samples (NVML, every CLOCK_INTERVAL_S, plus
+    one at each end) taken while the timed region runs; the timed region of a
+    default run lasts only ~12 ms.  The sampler is a child process, so that it
+    takes no time from this process's Python thread (the 1D step is bound by
+    host time), and it is started before the warm-up steps and only told when
+    to sample: a process spawned right before the timed steps measurably
+    slowed their launches (~5% of a 2D step)."""
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4}
 
     def __init__(self, index):
-        self.index = index
+        import subprocess
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(index),
+                                          str(CLOCK_INTERVAL_S)],
+                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            if self.proc.stdout.readline().strip() != "idle":
+                raise RuntimeError("clock sampler did not start")
+        except Exception:
+            self._kill()
+
+    def _kill(self):
+        if self.proc is not None:
+            self.proc.kill()
+            self.proc.wait()
         self.proc = None
 
     def start(self):
-        import subprocess
+        if self.proc is None:
+            return
         try:
-            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index)],
-                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+            self.proc.stdin.write("g")
+            self.proc.stdin.flush()
             if self.proc.stdout.readline().strip() != "ready":
-                raise RuntimeError("clock sampler did not start")
+                raise RuntimeError("clock sampler did not start sampling")
         except Exception:
-            if self.proc is not None:
-                self.proc.kill()
-                self.proc.wait()
-            self.proc = None
+            self._kill()
 
     def stop(self):
         if self.proc is None:
             return None
         try:
-            out, _ = self.proc.communicate("stop\n", timeout=30)
+            out, _ = self.proc.communicate("s", timeout=30)
             d = json.loads(out.strip().splitlines()[-1])
         except Exception:
-            self.proc.kill()
-            self.proc.wait()
+            self._kill()
             return None
         samples = d["s"]
         if not samples:
@@ -405,6 +423,9 @@ def run_ours(args, rank, world, local):
     from cpab import _native
 
     dev = torch.device("cuda", local)
+    # rank 0 samples the clocks; its sampler process starts now, long before
+    # the timed steps, and idles until they begin
+    clocks = Clocks(local) if rank == 0 else None
     w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev)
     default = args.config == "2d"
 
@@ -467,8 +488,7 @@ def run_ours(args, rank, world, local):
         dev_step()
     torch.cuda.synchronize()
 
-    clocks = Clocks(local)
-    if rank == 0:
+    if clocks is not None:
         clocks.start()
     if world > 1:
         dist.barrier()
@@ -486,7 +506,7 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.barrier()
     timings["on"] = False
-    clk = clocks.stop() if rank == 0 else None
+    clk = clocks.stop() if clocks is not None else None
     total_ms = sum(s.elapsed_time(e) for s, e in ev)
     kern = {k: sum(s.elapsed_time(e) for s, e in v) / max(len(v), 1) for k, v in timings.items()
             if k != "on"}
