@@ -48,3 +48,30 @@ def test_default_config_record(world):
     assert cfg["global_batch"] == bench.BATCH * bench.N_POINTS * world
     assert cfg["point_order"] == bench.ORDER_NOTE
     assert "flushed" in cfg["l2"]
+
+
+def _run_reference_arm(env_extra):
+    import json
+    import subprocess
+    env = dict(os.environ, **env_extra)
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                        "--steps", "1", "--warmup", "1"], capture_output=True, text=True,
+                       env=env, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    return [json.loads(ln) for ln in lines]
+
+
+def test_reference_arm_prints_one_line_on_rank0():
+    """The CPU reference arm (the oracle port on host threads) prints one JSON
+    line with the same metric/config as our arm, and e2e without copies."""
+    (line,) = _run_reference_arm({"RANK": "0", "WORLD_SIZE": "1"})
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["config"] == bench.config(1) and line["higher_is_better"] is True
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"],
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["cpu_baseline"]["kind"] in ("port", "reference") and line["value"] > 0
+
+
+def test_reference_arm_other_ranks_do_nothing():
+    assert _run_reference_arm({"RANK": "1", "WORLD_SIZE": "2"}) == []
