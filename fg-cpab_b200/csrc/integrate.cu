@@ -408,7 +408,18 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     // 65535 cells, so a thread's record stays mostly in L1.  Full segments run
     // with compile-time trip counts; only the tail segment (T % S steps) is
     // guarded.
-    float ck[kMaxSegs][ND];
+    // 3D: with the cell record in shared memory, the segment checkpoints sit
+    // behind it ([seg][k][threads]); otherwise in local memory.
+    constexpr bool kCkSmem = ND == 3 && CL_SMEM;
+    float ck_local[kCkSmem ? 1 : kMaxSegs][ND];
+    float *s_ck = reinterpret_cast<float *>(
+                      reinterpret_cast<char *>(s_cl - threadIdx.x) +
+                      (((size_t)a.T * blockDim.x * sizeof(CellT) + 15) & ~(size_t)15)) +
+                  threadIdx.x;
+    auto ck = [&](int seg, int k) -> float & {
+      if constexpr (kCkSmem) return s_ck[(seg * ND + k) * blockDim.x];
+      else return ck_local[seg][k];
+    };
     CellT cl_local[(ADAPT || CL_SMEM) ? 1 : kMaxSteps];
     auto cl = [&](int step) -> CellT & {
       if constexpr (CL_SMEM) return s_cl[step * blockDim.x];
@@ -417,7 +428,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     auto phase1 = [&](int seg, auto tail) {
       constexpr bool kTail = decltype(tail)::value;
 #pragma unroll
-      for (int k = 0; k < ND; ++k) ck[seg][k] = p[k];
+      for (int k = 0; k < ND; ++k) ck(seg, k) = p[k];
 #pragma unroll
       for (int s = 0; s < S; ++s) {
         if (kTail && s >= rem) break;
@@ -446,7 +457,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
       float xs[S][ND];
       int cs[S];
 #pragma unroll
-      for (int k = 0; k < ND; ++k) p[k] = ck[seg][k];
+      for (int k = 0; k < ND; ++k) p[k] = ck(seg, k);
 #pragma unroll
       for (int s = 0; s < S; ++s) {
         if (kTail && s >= rem) break;
@@ -709,6 +720,18 @@ cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
               : launch_wave(k_forward<ND, false, false>, kFwdThreads, 0, a, s);
 }
 
+// Shared memory of the per-step cell record, plus in 3D the segment
+// checkpoints that the backward keeps beside it (3D tables stay in global
+// memory, so shared memory has room; in local memory the checkpoints competed
+// with the table rows for L1).
+template <int ND, typename CellT>
+size_t cell_record_bytes(int threads, int T) {
+  size_t b = (size_t)threads * T * sizeof(CellT);
+  b = (b + 15) & ~(size_t)15;
+  if constexpr (ND == 3) b += (size_t)((T + kSegSteps - 1) / kSegSteps) * ND * sizeof(float) * threads;
+  return b;
+}
+
 template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, typename CellT>
 cudaError_t backward_launch(const IntegrateArgs &a, size_t smem, size_t cl, cudaStream_t s) {
   constexpr int kT = BwdShape<ND>::kThreads;
@@ -743,7 +766,7 @@ cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
   constexpr int kT = BwdShape<ND>::kThreads;
   // Shared memory, in order of preference: the cell table, the 1D moment
   // table, the 16-bit cell record (when all of it fits the budget).
-  const size_t cl_bytes = (ADAPT || sizeof(CellT) != 2) ? 0 : (size_t)kT * a.T * sizeof(CellT);
+  const size_t cl_bytes = (ADAPT || sizeof(CellT) != 2) ? 0 : cell_record_bytes<ND, CellT>(kT, a.T);
   auto cl_fits = [&](size_t used) { return used + cl_bytes <= kBwdSmemBudget ? cl_bytes : 0; };
   if constexpr (ND == 1) {
     if (2 * tab <= kBwdSmemBudget)
@@ -772,7 +795,7 @@ cudaError_t mesh_backward_cells(const IntegrateArgs &a, const MeshArgs &m, cudaS
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
   constexpr int kT = BwdShape<ND>::kThreads;
   constexpr bool kCl = !ADAPT && sizeof(CellT) == 2;
-  const size_t cl = kCl ? (size_t)kT * a.T * sizeof(CellT) : 0;
+  const size_t cl = kCl ? cell_record_bytes<ND, CellT>(kT, a.T) : 0;
   if (tab <= kBwdSmemBudget) {
     if constexpr (kCl) {
       if (tab + cl <= kBwdSmemBudget)
