@@ -6,8 +6,8 @@ cpab/pytorch/transformer_cuda.cpp:171-178).  ``cpab_gpu`` below offers the
 same five functions -- same arguments, shapes, output allocation
 (``torch.zeros`` on the current CUDA device) and RuntimeError on bad input --
 implemented over libcpab_b200's C ABI, so that the reference's transformer.py
-can switch backends by replacing its ``load(...)`` call (see
-INTEGRATION.md).  The module also works when loaded by file path from
+can switch backends by replacing its ``load(...)`` call with an import of
+this module.  The module also works when loaded by file path from
 another package (it then loads _native.py next to it the same way), so the
 reference's own ``cpab`` package can use it without a name clash.
 """

@@ -20,12 +20,15 @@ _DEVICE = torch.device("cuda")
 class Cpab(object):
     """Continuous piecewise-affine transformations with a B200 (sm_100a) backend.
 
-    Arguments:
-        tess_size: list of 1, 2, or 3 integers defining the number of cells
-            per spatial dimension
-        zero_boundary: bool, whether the boundary velocity is constrained to 0
-        volume_perservation: bool, whether the transform is volume preserving
-        override: bool, whether to rebuild and overwrite the cached basis
+    The velocity field is affine on each cell of a regular tessellation of
+    [0, 1]^ndim (intervals, four triangles per square, or five tetrahedra per
+    cube) and continuous across cells; ``theta`` holds its coordinates in the
+    basis of that space.
+
+    tess_size -- cells per axis, a list or tuple of 1 to 3 positive ints
+    zero_boundary -- pin the velocity to zero on the domain's boundary
+    volume_perservation -- restrict the field to divergence-free ones
+    override -- recompute the basis even when a cached file exists
     """
 
     def __init__(self, tess_size, zero_boundary=True, volume_perservation=False, override=False):
@@ -161,14 +164,12 @@ class Cpab(object):
         return torch.zeros(n_sample, self.params.d, dtype=torch.float32, device=_DEVICE) + epsilon
 
     def transform_grid(self, grid, theta):
-        """Integrate a grid using the transformation parameters in ``theta``.
+        """Move every point of ``grid`` along the flow of each transformation.
 
-        Arguments:
-            grid: [ndim, n_points] matrix or [n_batch, ndim, n_points] tensor
-            theta: [n_batch, d] matrix
-
-        Output:
-            transformed_grid: [n_batch, ndim, n_points] tensor
+        ``grid`` is shared by all transformations as [ndim, n_points], or
+        given per transformation as [n_batch, ndim, n_points]; ``theta`` is
+        [n_batch, d].  Returns the end points, [n_batch, ndim, n_points],
+        differentiable in ``theta`` and in ``grid``.
         """
         if len(grid.shape) == 3:
             assert grid.shape[0] == theta.shape[0], \
@@ -176,15 +177,13 @@ class Cpab(object):
         return transformer(grid, theta, self.params, compute_points_grad=True)
 
     def transform_grid_chain(self, grid, theta_chain, scale_by_dt=False):
-        """Apply a time-ordered chain of CPAB transforms to a grid.
+        """Compose several transformations: stage i moves the output of stage i-1.
 
-        Arguments:
-            grid: [ndim, n_points] or [n_batch, ndim, n_points] tensor
-            theta_chain: [n_transforms, d] or [n_transforms, n_batch, d] tensor
-            scale_by_dt: bool, multiply each stage's theta by 1/n_transforms
-
-        Output:
-            transformed_grid: [n_batch, ndim, n_points] tensor
+        ``theta_chain`` is [n_stages, d] (one transformation per stage) or
+        [n_stages, n_batch, d]; ``grid`` is laid out as in transform_grid.
+        With ``scale_by_dt`` every stage's theta is divided by n_stages, so
+        that the chain integrates over unit time in total.  Returns
+        [n_batch, ndim, n_points].
         """
         assert type(scale_by_dt) == bool, "scale_by_dt must be bool"
         assert theta_chain.dim() in (2, 3), \
@@ -234,14 +233,9 @@ class Cpab(object):
         assert type(override) == bool, "override must be True or False"
 
     def __repr__(self):
-        return f'''
-        CPAB transformer class ({self.params.ndim}D, sm_100a backend).
-            Parameters:
-                Tesselation size:           {self.params.nc}
-                Total number of cells:      {self.params.nC}
-                Theta size:                 {self.params.d}
-                Domain lower bound:         {self.params.domain_min}
-                Domain upper bound:         {self.params.domain_max}
-                Zero Boundary:              {self.params.zero_boundary}
-                Volume perservation:        {self.params.volume_perservation}
-        '''
+        p = self.params
+        rows = [("dimensions", p.ndim), ("cells per axis", p.nc), ("cells", p.nC),
+                ("theta length d", p.d), ("domain", "%s to %s" % (p.domain_min, p.domain_max)),
+                ("zero boundary", p.zero_boundary),
+                ("volume preserving", p.volume_perservation)]
+        return "Cpab (sm_100a backend)\n" + "\n".join("  %-18s %s" % r for r in rows)

@@ -258,6 +258,9 @@ int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points, int
   if (ndim < 1 || ndim > 3) return fail(CPAB_ERR_ARG, "order_points: ndim must be 1, 2 or 3");
   const int64_t nC = cell_count(ndim, nc);
   if (nC <= 0) return fail(CPAB_ERR_ARG, "order_points: tessellation sizes must be in [1, 2^20]");
+  // Same cell limit as the integrators; the kernels index cells with int.
+  if (nC > (1 << 26))
+    return fail(CPAB_ERR_SIZE, "order_points: too many cells (%lld)", (long long)nC);
   if (nP < 0 || n_sets < 0) return fail(CPAB_ERR_ARG, "order_points: negative size");
   if (n_sets > 65535) return fail(CPAB_ERR_SIZE, "order_points: more than 65535 point sets");
   if (nP > INT32_MAX) return fail(CPAB_ERR_SIZE, "order_points: more than 2^31-1 points");

@@ -21,7 +21,10 @@
 // it is never handed to a kernel directly: the first call on each device (with
 // that device current) asks the runtime for the array's device address with
 // cudaGetSymbolAddress and keeps it.  That first call should therefore come
-// before any stream capture on that device.
+// before any stream capture on that device.  The kept address belongs to the
+// device's current context: after cudaDeviceReset (or anything else that
+// destroys and recreates the primary context) it is stale, so this entry
+// point must not be used on that device again in the same process.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -60,19 +63,27 @@ cudaError_t static_counts(int32_t **out) {
 extern "C" int cpab_b200_order_points_static(int ndim, const int32_t *nc, const float *points,
                                              int64_t nP, int n_sets, int32_t *order,
                                              cpab_stream_t stream) {
-  // Sizes first (nothing touches the GPU before they pass); invalid shapes are
-  // reported by cpab_b200_order_points itself below.
+  // Sizes first (nothing touches the GPU before they pass); invalid shapes
+  // (an axis outside [1, 2^20], as cpab_b200_order_points checks) leave nC at
+  // 0 and are reported by cpab_b200_order_points itself below.  With every
+  // axis at most 2^20, nC <= 5 * 2^60 fits int64; the limit is tested by
+  // division so that n_sets * nC is never formed.
   int64_t nC = 0;
   if (ndim >= 1 && ndim <= 3 && nc != nullptr) {
-    nC = 1;
-    for (int k = 0; k < ndim; ++k) nC *= nc[k] > 0 ? nc[k] : 0;
-    nC *= ndim == 1 ? 1 : (ndim == 2 ? 4 : 5);
+    nC = ndim == 1 ? 1 : (ndim == 2 ? 4 : 5);
+    for (int k = 0; k < ndim; ++k) {
+      if (nc[k] < 1 || nc[k] > (1 << 20)) {
+        nC = 0;
+        break;
+      }
+      nC *= nc[k];
+    }
   }
-  if (nC > 0 && n_sets > 0 && nP > 0 && (int64_t)n_sets * nC > kStaticCounts)
+  if (nC > 0 && n_sets > 0 && nP > 0 && nC > kStaticCounts / n_sets)
     return cpab::report_error(CPAB_ERR_SIZE,
-                              "order_points_static: n_sets * nC = %lld exceeds the built-in "
+                              "order_points_static: n_sets (%d) * nC (%lld) exceeds the built-in "
                               "scratch of %lld counters; use cpab_b200_order_points",
-                              (long long)((int64_t)n_sets * nC), (long long)kStaticCounts);
+                              n_sets, (long long)nC, (long long)kStaticCounts);
   int32_t *counts = nullptr;
   if (nC > 0 && n_sets > 0 && nP > 0) {
     const cudaError_t e = static_counts(&counts);

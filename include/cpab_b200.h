@@ -153,7 +153,9 @@ int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points,
  * array built into the library, present on every GPU that loads it; n_sets * nC
  * may not exceed 2^20 (CPAB_ERR_SIZE otherwise).  All calls on a device share
  * that array: calls whose GPU work overlaps race.  The first call on a device
- * looks up the array's device address, so make it before any stream capture.
+ * looks up the array's device address, so make it before any stream capture;
+ * the address is kept for the life of the process, so after cudaDeviceReset
+ * (a new primary context) this entry point must not be used on that device.
  * No counterpart in the reference.
  */
 int cpab_b200_order_points_static(int ndim, const int32_t *nc,

@@ -18,7 +18,11 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_CORE = os.environ.get("CPAB_REFERENCE_CORE", "/root/reference/cpab/core")
+# The reference checkout: $CPAB_REFERENCE, else a sibling of this repository
+# named "reference".
+REF_ROOT = os.path.normpath(os.environ.get(
+    "CPAB_REFERENCE", os.path.join(os.path.dirname(HERE), os.pardir, "reference")))
+REF_CORE = os.environ.get("CPAB_REFERENCE_CORE", os.path.join(REF_ROOT, "cpab", "core"))
 REF_DIR = os.path.join(HERE, "_ref")
 
 

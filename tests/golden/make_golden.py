@@ -2,8 +2,8 @@
 
     python tests/golden/make_golden.py [path/to/reference]
 
-Needs the reference source tree (the path argument; its default is the checkout
-location this build used); it is copied to a
+Needs the reference source tree: the path argument, else $CPAB_REFERENCE, else
+a directory "reference" beside this repository.  It is copied to a
 temporary directory first because constructing a reference tessellation writes
 a basis cache next to the package.  The reference's cpab/__init__.py
 JIT-compiles CUDA, so cpab.core and cpab.pytorch.interpolation are loaded as
@@ -61,7 +61,11 @@ def case_key(nc, zb, vp):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    # The reference checkout: first argument, else $CPAB_REFERENCE, else a
+    # sibling of this repository named "reference".
+    ref_root = (sys.argv[1] if len(sys.argv) > 1 else
+                os.environ.get("CPAB_REFERENCE",
+                               os.path.join(HERE, os.pardir, os.pardir, os.pardir, "reference")))
     tmp, tess, interp = load_reference(ref_root)
     import torch
 

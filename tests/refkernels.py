@@ -18,6 +18,31 @@ def available():
     return os.path.exists(PATH)
 
 
+def reference_present():
+    """True when the reference's kernel sources are on this machine (where
+    oracle/build_oracle.py --ref would build oracle/_ref)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "cpab_oracle_build", os.path.join(ROOT, "oracle", "build_oracle.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return os.path.exists(os.path.join(mod.REF_CORE, "cpab_ops_2d.cu"))
+
+
+def require():
+    """Skip when the reference kernels cannot exist here (no build, no
+    sources: the GPU box without a prebuilt oracle/_ref); fail when the
+    sources are present but the build is missing, so that a forgotten build
+    does not pass as a silent skip."""
+    import pytest
+    if available():
+        return
+    if reference_present():
+        pytest.fail("the reference sources are present but oracle/_ref/libcpab_ref.so is not "
+                    "built: run python oracle/build_oracle.py --ref")
+    pytest.skip("oracle/_ref not built and the reference sources are absent")
+
+
 def lib():
     global _lib
     if _lib is None:

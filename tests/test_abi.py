@@ -84,6 +84,29 @@ def test_other_entry_points_validate():
     assert L.cpab_b200_forward_1d_closed_form(P, 10, 0, None, P, 1, 0, P, None) == -1
 
 
+def test_order_points_rejects_huge_tessellations_before_any_gpu_work():
+    """Axes within the per-axis limit can still multiply to more cells than
+    the sort indexes (int) or than the built-in scratch holds; both entry
+    points must refuse on the host (no CUDA call: these run without a GPU)."""
+    L = _native.lib()
+    err = lambda: L.cpab_b200_last_error().decode()  # noqa: E731
+    nc2 = (ctypes.c_int32 * 2)(1 << 20, 1 << 20)        # 4 * 2^40 cells
+    assert L.cpab_b200_order_points(2, nc2, P, 10, 1, P, P, None) == -4
+    assert "too many cells" in err()
+    nc3 = (ctypes.c_int32 * 3)(1 << 20, 1 << 20, 1 << 20)  # 5 * 2^60 cells
+    assert L.cpab_b200_order_points(3, nc3, P, 10, 1, P, P, None) == -4
+    # n_sets * nC would overflow int64 if formed; the static variant must
+    # still report its scratch limit, not reach the GPU.
+    assert L.cpab_b200_order_points_static(3, nc3, P, 10, 2, P, None) == -4
+    assert "exceeds the built-in scratch" in err()
+    assert L.cpab_b200_order_points_static(3, nc3, P, 10, 65535, P, None) == -4
+    over = (ctypes.c_int32 * 2)((1 << 20) + 1, 4)       # one axis beyond 2^20
+    assert L.cpab_b200_order_points_static(2, over, P, 10, 1, P, None) == -1
+    assert "[1, 2^20]" in err()
+    nc = (ctypes.c_int32 * 2)(512, 512)                 # 2^20 cells: fits once, not twice
+    assert L.cpab_b200_order_points_static(2, nc, P, 10, 2, P, None) == -4
+
+
 def test_transform_data_entry_points_validate():
     L = _native.lib()
     sz = (ctypes.c_int64 * 2)(8, 8)

@@ -11,8 +11,14 @@ from oracle import oracle as O
 from helpers import X_ATOL, cpab, near_boundary, rand_points, rand_theta, rel_l2
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU"),
-              pytest.mark.skipif(not R.available(), reason="oracle/_ref not built")]
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+
+@pytest.fixture(autouse=True)
+def _reference_kernels_built():
+    R.require()
+
+
 DEV = "cuda"
 
 CASES = [((50,), True, 4, 20000, False, False, 50),

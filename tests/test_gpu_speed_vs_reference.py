@@ -20,8 +20,12 @@ from cpab.pytorch.transformer import device_basis
 from helpers import cpab
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU"),
-              pytest.mark.skipif(not R.available(), reason="oracle/_ref not built")]
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+
+@pytest.fixture(autouse=True)
+def _reference_kernels_built():
+    R.require()
 
 
 def _time(fn, reps=10):

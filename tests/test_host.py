@@ -19,7 +19,7 @@ def test_params_fields_match_reference_layout():
     assert p.Ashape == [2, 3] and p.nstepsolver == 50 and p.adaptive_substeps is False
     assert T.get_theta_dim() == 1522 and T.get_basis() is p.basis
     assert p.zero_boundary and not p.valid_outside
-    assert "Theta size" in repr(T)
+    assert "theta length d" in repr(T)
 
 
 def test_constraint_matrix_is_lazy():
