@@ -34,10 +34,11 @@ def sample(n, k, seed):
     return np.sort(np.random.default_rng(seed).choice(n, size=k, replace=False))
 
 
-def test_bench_2d_config_forward_and_gradient_at_full_size():
-    # Cpab([20,20]), batch 16, 125,000 points, theta ~ N(0,1).
-    C = cpab((20, 20), True)
-    nc = [20, 20]
+@pytest.mark.parametrize("nc", [[20, 20], [12, 12], [30, 30]], ids=["20x20", "12x12", "30x30"])
+def test_bench_2d_config_forward_and_gradient_at_full_size(nc):
+    # Cpab([20,20]), batch 16, 125,000 points, theta ~ N(0,1);
+    # the same workload is repeated at tessellations 12x12 and 30x30.
+    C = cpab(tuple(nc), True)
     B, nP = 16, 125_000
     th = torch.randn(B, C.params.d, generator=gen(0))
     pts = torch.rand(2, nP, generator=gen(1))
@@ -152,5 +153,81 @@ def test_dense_2d_transform_data_config_at_full_size():
     g[:, :, pix] = gs
     (out * torch.from_numpy(g.reshape(B, Ch, n, n)).to(DEV)).sum().backward()
     dgrid, _ = O.interpolate_backward(2, data.numpy(), x, (1, len(pix)), gs[:, :, None, :])
+    dth_ref, _ = O.gradient(nc, C.params.basis, pts, As_h, dgrid, T)
+    assert rel_l2(th_d.grad.cpu().numpy(), dth_ref) < DTHETA_RTOL
+
+
+def test_1d_config_at_full_size():
+    # Cpab([50], zero_boundary=True), batch 8, theta ~ N(0,1),
+    # 100,000 shared points ~ U[0,1]; loss sum((x_t - x)^2).  The forward is the
+    # closed-form integration (cpab/core/cpab_ops_1d.cu:131-205).
+    C = cpab((50,), True)
+    nc = [50]
+    B, nP = 8, 100_000
+    th = torch.randn(B, C.params.d, generator=gen(0))
+    pts = torch.rand(1, nP, generator=gen(1))
+    th_d = th.to(DEV).requires_grad_(True)
+    pts_d = pts.to(DEV)
+    out = C.transform_grid(pts_d, th_d)
+
+    As, _ = _native.build_A(1, C.params.nC, device_basis(C.params, th_d.device),
+                            th_d.detach(), 1.0 / T)
+    As_h = As.cpu().numpy()
+    idx = sample(nP, 4000, 21)
+    ref = O.integrate(nc, pts[:, idx].numpy(), As_h, None, T)
+    got = out.detach()[:, :, idx].cpu().numpy()
+    assert np.abs(got - ref).max() <= X_ATOL
+    flat_g, flat_r = got.reshape(1, -1), ref.reshape(1, -1)
+    differ = O.cells(nc, flat_g) != O.cells(nc, flat_r)
+    assert not (differ & ~near_boundary(nc, flat_r, BOUNDARY_EPS)).any()
+
+    # the bench's loss, with its upstream gradient 2 (x_t - x) kept on a sample only
+    sub = sample(nP, 1000, 22)
+    mask = torch.zeros(1, 1, nP)
+    mask[:, :, sub] = 1.0
+    loss = (((out - pts_d) ** 2) * mask.to(DEV)).sum()
+    loss.backward()
+    x_sub = O.integrate(nc, pts[:, sub].numpy(), As_h, None, T)
+    w = (2.0 * (x_sub - pts[:, sub].numpy()[None])).astype(np.float32)
+    dth_ref, _ = O.gradient(nc, C.params.basis, pts[:, sub].numpy(), As_h, w, T)
+    assert rel_l2(th_d.grad.cpu().numpy(), dth_ref) < DTHETA_RTOL
+
+
+def test_3d_transform_data_config_at_full_size():
+    # BASELINE 3D: Cpab([10,10,10], zero_boundary=True), batch 4, theta ~ N(0,1),
+    # single-channel 128^3 volumes, each a seeded sum of 20 Gaussian blobs;
+    # transform_data to [128, 128, 128] (trilinear).  The reference composes
+    # uniform_meshgrid, transform_grid and interpolate (cpab/cpab.py:306-308,
+    # cpab/pytorch/interpolation.py:97-160); this library runs it fused.
+    import bench
+    C = cpab((10, 10, 10), True)
+    nc = [10, 10, 10]
+    B, n = 4, 128
+    th = torch.randn(B, C.params.d, generator=gen(0))
+    g = gen(2)
+    data = torch.stack([bench.blobs([n, n, n], g) for _ in range(B)])[:, None]
+    th_d = th.to(DEV).requires_grad_(True)
+    out = C.transform_data(data.to(DEV), th_d, (n, n, n))
+    assert out.shape == (B, 1, n, n, n)
+
+    As, trels = _native.build_A(3, C.params.nC, device_basis(C.params, th_d.device),
+                                th_d.detach(), 1.0 / T)
+    As_h, tr_h = As.cpu().numpy(), trels.cpu().numpy()
+    axes = mesh_axes(C.params, (n, n, n), th_d.device).cpu().numpy()
+    vox = sample(n ** 3, 1500, 31)          # output voxels o = (i0 * n + i1) * n + i2
+    i0, i1, i2 = vox // (n * n), (vox // n) % n, vox % n
+    pts = np.stack([axes[i0], axes[n + i1], axes[2 * n + i2]]).astype(np.float32)
+    x = O.integrate(nc, pts, As_h, tr_h, T)                      # [B, 3, 1500]
+    ref = O.interpolate(3, data.numpy(), x, (1, 1, len(vox)))     # [B, 1, 1, 1, 1500]
+    got = out.detach().reshape(B, 1, -1)[:, :, vox].cpu().numpy()
+    assert np.abs(got - ref[:, :, 0, 0]).max() <= 1e-5
+
+    # upstream gradient on the sampled voxels only
+    gr = np.zeros((B, 1, n ** 3), np.float32)
+    gs = np.random.default_rng(32).uniform(-1, 1, (B, 1, len(vox))).astype(np.float32)
+    gr[:, :, vox] = gs
+    (out * torch.from_numpy(gr.reshape(B, 1, n, n, n)).to(DEV)).sum().backward()
+    dgrid, _ = O.interpolate_backward(3, data.numpy(), x, (1, 1, len(vox)),
+                                      gs[:, :, None, None, :])
     dth_ref, _ = O.gradient(nc, C.params.basis, pts, As_h, dgrid, T)
     assert rel_l2(th_d.grad.cpu().numpy(), dth_ref) < DTHETA_RTOL
