@@ -68,6 +68,17 @@ def profiled(key):
     return None
 
 
+def profiled_str(key):
+    """A text field of the committed ncu summary, or None."""
+    try:
+        for line in open(PROFILE):
+            if line.startswith(key + ":"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 ORDER_NOTE = "points sorted by cell inside every timed step (no order kept across steps)"
 MESH_ORDER_NOTE = ("meshgrid points generated in the kernels; 3D visits them in a cell order "
                    "that depends only on the tessellation and output size, computed once")
@@ -102,24 +113,32 @@ def sample():
     except Exception:
         pass
 print("idle", flush=True)
-os.read(0, 1)                      # "g": the timed region starts
-sample()
-print("ready", flush=True)
-while not select.select([0], [], [], float(sys.argv[2]))[0]:
+# commands on stdin: "g" start/resume sampling, "p" pause, "s" stop and report
+cmd = os.read(0, 1)
+while cmd == b"g":
     sample()
-sample()
+    print("ready", flush=True)
+    while not select.select([0], [], [], float(sys.argv[2]))[0]:
+        sample()
+    sample()
+    cmd = os.read(0, 1)
+    if cmd == b"p":
+        print("paused", flush=True)
+        cmd = os.read(0, 1)
 print(json.dumps(out), flush=True)
 """
 
 
 class Clocks:
     """SM clock and throttle-reason samples (NVML, every CLOCK_INTERVAL_S, plus
-    one at each end) taken while the timed region runs; the timed region of a
-    default run lasts only ~12 ms.  The sampler is a child process, so that it
-    takes no time from this process's Python thread (the 1D step is bound by
-    host time), and it is started before the warm-up steps and only told when
-    to sample: a process spawned right before the timed steps measurably
-    slowed their launches (~5% of a 2D step)."""
+    one at each end of every sampled stretch) taken while the timed regions
+    run: the device-resident steps, the end-to-end steps and the graph
+    replays, paused in between (a default run's regions last ~12 ms each).
+    The sampler is a child process, so that it takes no time from this
+    process's Python thread (the 1D step is bound by host time), and it is
+    started before the warm-up steps and only told when to sample: a process
+    spawned right before the timed steps measurably slowed their launches
+    (~5% of a 2D step)."""
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4}
 
@@ -142,16 +161,23 @@ class Clocks:
             self.proc.wait()
         self.proc = None
 
-    def start(self):
+    def _send(self, cmd, reply):
         if self.proc is None:
             return
         try:
-            self.proc.stdin.write("g")
+            self.proc.stdin.write(cmd)
             self.proc.stdin.flush()
-            if self.proc.stdout.readline().strip() != "ready":
-                raise RuntimeError("clock sampler did not start sampling")
+            if self.proc.stdout.readline().strip() != reply:
+                raise RuntimeError("clock sampler did not answer %r" % cmd)
         except Exception:
             self._kill()
+
+    def start(self):
+        """Start (or resume) sampling."""
+        self._send("g", "ready")
+
+    def pause(self):
+        self._send("p", "paused")
 
     def stop(self):
         if self.proc is None:
@@ -382,7 +408,7 @@ def blobs(shape, g, n=20):
     return vol
 
 
-def graph_replay(step, resident, C, flush, steps, warmup):
+def graph_replay(step, resident, C, flush, steps, warmup, clocks=None):
     """ms per replay of the device-resident step captured in one CUDA graph."""
     from cpab.pytorch.transformer import clear_order_cache
 
@@ -406,17 +432,233 @@ def graph_replay(step, resident, C, flush, steps, warmup):
     for _ in range(max(warmup, 1)):
         g.replay()
     torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
+    ms = timed_steps(g.replay, steps, flush, 1)
+    if clocks is not None:
+        clocks.pause()
+    del g
+    return ms
+
+
+# Native calls of the library timed per phase (CUDA events on the stream each
+# is enqueued on) and the kernels each launches.
+KERNELS_PER_CALL = {"build_A": 1, "order_points": 3, "project": 1, "interpolate": 1,
+                    "interpolate_backward": 1, "expm": 1, "forward": 1, "backward": 1,
+                    "transform_data": 1, "transform_data_backward": 1, "forward_chain": 1,
+                    "backward_chain": 1}
+
+
+class PhaseTimer:
+    """Wraps the library's native calls (and torch.distributed.all_reduce)
+    with CUDA events while `rec` names a dict to record into; also counts the
+    kernels of this library that the recorded calls launch."""
+
+    def __init__(self, native):
+        self.rec = None
+        self.only = None       # names to time (None: all); the others are only counted
+        self.capture = False
+        self.launches = 0
+        for name in KERNELS_PER_CALL:
+            setattr(native, name, self._wrap(name, getattr(native, name), True))
+        dist.all_reduce = self._wrap("allreduce", dist.all_reduce, False)
+
+    def _wrap(self, name, fn, ours):
+        def call(*a, **k):
+            rec = self.rec
+            if rec is None or self.capture:
+                return fn(*a, **k)
+            if ours:
+                self.launches += KERNELS_PER_CALL[name]
+            if self.only is not None and name not in self.only:
+                return fn(*a, **k)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = fn(*a, **k)
+            e.record()
+            rec.setdefault(name, []).append((s, e))
+            return r
+        return call
+
+
+def phase_ms(rec, steps, world):
+    """Mean ms per step of every recorded phase, max over ranks."""
+    names = sorted(rec)
+    if world > 1:  # every rank reports the same phases, in the same order
+        names = sorted(set(names) | {"allreduce"})
+    return {n: max_over_ranks(sum(s.elapsed_time(e) for s, e in rec.get(n, [])) / steps, world)
+            for n in names}
+
+
+def timed_steps(fn, steps, flush, world):
+    """ms per step of fn() over `steps` calls: CUDA events per step, L2
+    flushed before each (untimed), barrier + synchronize on both sides, max
+    over ranks."""
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     ev = []
     for _ in range(steps):
         flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        g.replay()
+        fn()
         e.record()
         ev.append((s, e))
     torch.cuda.synchronize()
-    del g
-    return sum(s.elapsed_time(e) for s, e in ev) / steps
+    if world > 1:
+        dist.barrier()
+    return max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world) / steps
+
+
+def source_sha():
+    """Hash of the sources of the integration kernels (k_forward, k_backward):
+    profiles/ summaries record it, so a figure profiled from other sources is
+    not reported as this build's."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("cpab_device.cuh", "integrate.cu", "launch.h"):
+        with open(os.path.join(ROOT, "fg-cpab_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
+def profile_record():
+    """(traffic bytes, warp instructions, provenance) of the committed ncu
+    summary of k_backward on the bench workload; the figures are None when
+    the summary was made from other kernel sources than these."""
+    sha = profiled_str("source_sha")
+    prov = {"file": os.path.relpath(PROFILE, ROOT), "source_sha": sha,
+            "commit": profiled_str("commit"), "current_source_sha": source_sha()}
+    if sha is None or sha != prov["current_source_sha"]:
+        prov["stale"] = True
+        return None, None, prov
+    return profiled("traffic_bytes_per_launch"), profiled("warp_instructions_per_launch"), prov
+
+
+def breakdown(fn, steps, flush, world, timer):
+    """Per-phase ms of fn (every native call and allreduce bracketed by
+    events), from a pass of its own, so that the events' host time does not
+    enter the step times reported beside it."""
+    rec = {}
+    timer.rec, timer.only = rec, None
+    n0 = timer.launches
+    timed_steps(fn, steps, flush, world)
+    timer.rec = None
+    timer.launches = n0
+    return phase_ms(rec, steps, world)
+
+
+def strong_scaling(C, steps, warmup, flush, rank, world, timer):
+    """The fixed 2D problem (125,000 points x batch 16) split over the ranks
+    two ways: points sharded with one dtheta allreduce per step, and the batch
+    sharded (16 / world transformations per rank, no collective).  Returns
+    one record per way with the per-phase breakdown of rank max times."""
+    from cpab.distributed import shard_points, transform_grid_sharded
+    from cpab.pytorch.transformer import clear_order_cache
+    dev = torch.device("cuda", torch.cuda.current_device())
+    group = dist.group.WORLD
+    theta = torch.randn(BATCH, C.params.d, generator=torch.Generator().manual_seed(0)).to(dev)
+    pts = torch.rand(2, N_POINTS, generator=torch.Generator().manual_seed(1))
+    mine = shard_points(pts, rank, world).to(dev)
+    full = pts.to(dev)
+    n_total = BATCH * N_POINTS * 2
+    out = {}
+
+    def points_step():
+        clear_order_cache(C.params)
+        t = theta.detach().requires_grad_(True)
+        o = transform_grid_sharded(C, mine, t, group)
+        # the global mean over all ranks' points, as one process would compute it
+        (((o - mine) ** 2).sum() / n_total).backward()
+
+    lo, hi = BATCH * rank // world, BATCH * (rank + 1) // world
+
+    def batch_step():
+        clear_order_cache(C.params)
+        t = theta[lo:hi].detach().requires_grad_(True)
+        o = C.transform_grid(full, t)
+        (((o - full) ** 2).sum() / n_total).backward()
+
+    for name, fn in (("points_sharded", points_step), ("batch_sharded", batch_step)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        ms = timed_steps(fn, steps, flush, world)
+        out[name] = {"value": BATCH * N_POINTS / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+                     "phase_ms": breakdown(fn, steps, flush, world, timer)}
+    out["points_sharded"]["how"] = ("the 125,000 points split over the ranks, all 16 "
+                                    "transformations on every rank, one dtheta allreduce")
+    out["batch_sharded"]["how"] = ("all 125,000 points on every rank, %d of the 16 "
+                                   "transformations per rank, no collective"
+                                   % (BATCH // world))
+    out["problem"] = "fixed: 125,000 points x batch 16 (2,000,000 pairs) whatever the GPU count"
+    return out
+
+
+REF_KERNELS = os.path.join(ROOT, "oracle", "_ref", "libcpab_ref.so")
+
+
+def ref_gpu_kernels(C, host, steps, warmup, flush):
+    """Baseline leg: the reference's own CUDA kernels (cpab/core/cpab_ops_2d.cu,
+    compiled unmodified for sm_100a into oracle/_ref) and torch.sparse.mm for
+    the projection, as the reference's transformer.py composes them, timed
+    with CUDA events on the bench inputs (A from this library's build_A).
+    Not part of the measured product; None when that build is absent."""
+    if not os.path.exists(REF_KERNELS):
+        return None
+    import ctypes
+    L = ctypes.CDLL(REF_KERNELS)
+    i, f, p = ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+    L.ref_expm.argtypes = [i, p, i, f, p]
+    L.ref_forward.argtypes = [i, i, i, i, p, i, i, p, p, i, i, i, p]
+    L.ref_backward.argtypes = [i, i, i, i, i, p, i, i, p, i, p, i, i, p, p]
+    from cpab import _native
+    from cpab.pytorch.transformer import device_basis
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nx, ny = TESS
+    theta = host["theta"].to(dev)
+    pts = host["points"].to(dev)
+    nP = pts.shape[1]
+    nC = C.params.nC
+    basis = device_basis(C.params, dev)
+    As, _ = _native.build_A(2, nC, basis, theta, 1.0 / NSTEP)
+    g = torch.randn(BATCH, 2, nP, generator=torch.Generator().manual_seed(3)).to(dev)
+    Bt = C._get_basis_sparse_gpu(device=dev).transpose(0, 1).coalesce()
+    trels = torch.zeros_like(As)
+    out = torch.zeros((BATCH, 2, nP), device=dev)
+    mom = torch.zeros((BATCH, nC, 6), device=dev)
+    gp = torch.zeros((BATCH, 2, nP), device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    torch.cuda.synchronize()
+    # the reference's launchers run on the legacy default stream; torch's
+    # default stream is that stream, so events recorded on it bracket them
+    calls = {
+        "expm": lambda: L.ref_expm(2, P(As), BATCH * nC, 1.0 / NSTEP, P(trels)),
+        "forward": lambda: L.ref_forward(2, nx, ny, 1, P(pts), nP, 0, P(trels), P(As), BATCH,
+                                         NSTEP, 0, P(out)),
+        "backward": lambda: L.ref_backward(2, nx, ny, 1, nC, P(pts), nP, 0, P(As), BATCH, P(g),
+                                           NSTEP, 0, P(mom), P(gp)),
+        "project": lambda: torch.sparse.mm(Bt, mom.reshape(BATCH, -1).t()).t().contiguous(),
+    }
+    res = {}
+    with torch.cuda.stream(torch.cuda.default_stream(dev)):
+        for name, fn in calls.items():
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(steps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                torch.cuda.synchronize()
+                ts.append(s.elapsed_time(e))
+            res[name] = statistics.median(ts)
+    res["fwd_grad_ms"] = res["expm"] + res["forward"] + res["backward"] + res["project"]
+    return res
 
 
 def run_ours(args, rank, world, local):
@@ -429,49 +671,13 @@ def run_ours(args, rank, world, local):
     w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev)
     default = args.config == "2d"
 
-    # Per-launch timing of the integration kernels, on the stream they run on
-    # (for transform_data the fused resample-integration kernels).
-    timings = {"forward": [], "backward": []}
     fused = getattr(w, "fused_data", None) is not None
     chain = w.stages > 1 and C.params.ndim in (2, 3)   # one launch through all stages
+    # the integration calls of this workload (for transform_data the fused
+    # resample-integration kernels)
     names = (("transform_data", "transform_data_backward") if fused else
              ("forward_chain", "backward_chain") if chain else ("forward", "backward"))
-    orig = {"forward": getattr(_native, names[0]), "backward": getattr(_native, names[1])}
-
-    def timed(name):
-        def call(*a, **k):
-            if timings.get("capture"):  # no timing events inside a CUDA graph capture
-                return orig[name](*a, **k)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            r = orig[name](*a, **k)
-            e.record()
-            if timings.get("on"):
-                timings[name].append((s, e))
-            return r
-        return call
-
-    setattr(_native, names[0], timed("forward"))
-    setattr(_native, names[1], timed("backward"))
-
-    # Kernels of this library launched inside the timed steps, counted per
-    # native call (order_points runs histogram, scan and scatter).
-    kernels_per_call = {"build_A": 1, "order_points": 3, "project": 1, "interpolate": 1,
-                        "interpolate_backward": 1, "expm": 1}
-    counted = {"n": 0}
-
-    def counting(name, fn):
-        def call(*a, **k):
-            if timings.get("on"):
-                counted["n"] += kernels_per_call.get(name, 1)
-            return fn(*a, **k)
-        return call
-
-    for name in kernels_per_call:
-        setattr(_native, name, counting(name, getattr(_native, name)))
-    for name in ("forward", "backward", "transform_data", "transform_data_backward",
-                 "forward_chain", "backward_chain"):
-        setattr(_native, name, counting(name, getattr(_native, name)))
+    timer = PhaseTimer(_native)
 
     resident = {k: v.to(dev) for k, v in host.items()}
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
@@ -490,29 +696,19 @@ def run_ours(args, rank, world, local):
 
     if clocks is not None:
         clocks.start()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    timings["on"] = True
-    ev = []
-    for _ in range(args.steps):
-        flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        dev_step()
-        e.record()
-        ev.append((s, e))
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    timings["on"] = False
-    clk = clocks.stop() if clocks is not None else None
-    total_ms = sum(s.elapsed_time(e) for s, e in ev)
-    kern = {k: sum(s.elapsed_time(e) for s, e in v) / max(len(v), 1) for k, v in timings.items()
-            if k != "on"}
-    total_ms = max_over_ranks(total_ms, world)
-    kern = {k: max_over_ranks(v, world) for k, v in kern.items()}
-    ms_step = total_ms / args.steps
+    # Events bracket the two integration kernels only (their mean launch time
+    # feeds the roofline); the other calls are counted.
+    rec = {}
+    timer.rec, timer.only = rec, set(names)
+    ms_step = timed_steps(dev_step, args.steps, flush, world)
+    timer.rec = None
+    launches = timer.launches
+    if clocks is not None:
+        clocks.pause()
+    kern = {k: max_over_ranks(sum(s.elapsed_time(e) for s, e in rec.get(n, [])) / args.steps,
+                              world)
+            for k, n in (("forward", names[0]), ("backward", names[1]))}
+    phases = breakdown(dev_step, args.steps, flush, world, timer)
     pairs_step = pairs_rank * world
     value = pairs_step / (ms_step * 1e-3)
 
@@ -532,31 +728,43 @@ def run_ours(args, rank, world, local):
     for _ in range(max(args.warmup, 1)):
         e2e_step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev = []
-    for _ in range(args.steps):
-        flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        e2e_step()
-        e.record()
-        ev.append((s, e))
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world) / args.steps
+    if clocks is not None:
+        clocks.start()
+    e2e_ms = timed_steps(e2e_step, args.steps, flush, world)
+    if clocks is not None:
+        clocks.pause()
 
     # One GPU: the same device-resident step captured once in a CUDA graph
     # (sort, forward, loss, backward, projection recorded; every replay runs
     # them all), which removes the host launch gaps between its kernels.
     graph_ms = None
     if world == 1 and not args.no_graph:
-        timings["capture"] = True
-        graph_ms = graph_replay(step, resident, C, flush, args.steps, args.warmup)
-        timings["capture"] = False
+        timer.capture = True
+        graph_ms = graph_replay(step, resident, C, flush, args.steps, args.warmup, clocks)
+        timer.capture = False
+    clk = clocks.stop() if clocks is not None else None
+
+    # N > 1, 2D 20x20: the fixed problem split over the ranks (strong scaling).
+    strong = None
+    if world > 1 and default and not args.no_strong:
+        strong = strong_scaling(C, args.steps, args.warmup, flush, rank, world, timer)
+
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = 4 + host["theta"].numel() * 4
+
+    # N = 1: the reference's own GPU kernels on the same inputs (baseline leg).
+    ref_kernels = None
+    if world == 1 and default and not args.no_ref_kernels:
+        ref_kernels = ref_gpu_kernels(C, host, args.steps, args.warmup, flush)
+        if ref_kernels is not None:
+            ours = {k: phases.get(k, 0.0) for k in ("build_A", "order_points", "forward",
+                                                    "backward", "project")}
+            ours["fwd_grad_ms"] = sum(ours.values())
+            ref_kernels = {
+                "what": "the reference's own CUDA kernels (cpab_ops_2d.cu, unmodified, sm_100a) "
+                        "+ torch.sparse.mm projection, CUDA-event medians on the bench inputs",
+                "reference_ms": ref_kernels, "ours_ms": ours,
+                "speedup_fwd_grad": ref_kernels["fwd_grad_ms"] / ours["fwd_grad_ms"]}
 
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -580,8 +788,7 @@ def run_ours(args, rank, world, local):
             bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
                          + 2 * w.batch * p.nC * ppc) * 4
         ach = bwd_bytes / (kern["backward"] * 1e-3) / 1e9
-        traffic = profiled("traffic_bytes_per_launch") if default else None
-        inst = profiled("warp_instructions_per_launch") if default else None
+        traffic, inst, prov = profile_record() if default else (None, None, None)
         clk_mhz = (clk or {}).get("sm_mhz") or 1965.0
         issue_peak = 4 * 148 * clk_mhz * 1e6
         issue = None
@@ -592,8 +799,7 @@ def run_ours(args, rank, world, local):
             issue_ach = inst / (kern["backward"] * 1e-3)
             issue = {"bound": "issue", "achieved": issue_ach, "peak": issue_peak,
                      "unit": "warp-inst/s", "frac": issue_ach / issue_peak,
-                     "inst_per_launch": inst, "sm_mhz": clk_mhz,
-                     "source": "profiles/k_backward_2d_20x20_b16_125k.md"}
+                     "inst_per_launch": inst, "sm_mhz": clk_mhz, "profile": prov}
         cfg = config(world) if default else {
             "workload": w.desc, "tess": w.tess, "batch": w.batch, "stages": w.stages,
             "nstepsolver": NSTEP, "global_batch": pairs_step, "parallelism": w.parallelism,
@@ -612,16 +818,24 @@ def run_ours(args, rank, world, local):
                          else "k_backward (fused adjoint)",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": bwd_bytes},
+                         "algorithmic_bytes_per_launch": bwd_bytes, "profile": prov},
             "issue_roofline": issue,
             "kernel_ms": kern,
+            "phase_ms": phases,
+            "phase_note": "mean ms per step of each native call (and allreduce), CUDA events "
+                          "in a separate pass of the same steps; the remainder of a step is "
+                          "torch's loss kernels and host launch gaps",
             "graph_replay": None if graph_ms is None else {
                 "value": pairs_step / (graph_ms * 1e-3), "unit": UNIT, "ms_per_step": graph_ms,
                 "note": "the value step captured once in a CUDA graph and replayed; "
                         "value and e2e above are eager"},
-            "gpu_launches": counted["n"],
+            "gpu_launches": launches,
             "clocks": clk,
         }
+        if strong is not None:
+            line["strong"] = strong
+        if ref_kernels is not None:
+            line["ref_kernels"] = ref_kernels
         if default and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(C.params.basis, host["theta"].numpy())
         emit(line)
@@ -652,6 +866,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the one-GPU CUDA graph replay measurement")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong-scaling figures of the N>1 default run")
+    ap.add_argument("--no-ref-kernels", action="store_true",
+                    help="skip timing the reference's own GPU kernels at N=1")
     ap.add_argument("--config", default="2d",
                     choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d"],
                     help="workload (default: BASELINE configs[1], 2D 20x20)")

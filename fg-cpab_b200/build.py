@@ -1,6 +1,10 @@
 """Builds libcpab_b200.so (the sm_100a kernels and their C ABI) in-tree.
 
-    python fg-cpab_b200/build.py [--force]
+    python fg-cpab_b200/build.py [--force] [--ptxas-v] [-DNAME=VALUE ... --out PATH]
+
+-D options set compile-time choices of the kernels (e.g. -DCPAB_MOMENT_FLUSH=1,
+see csrc/cpab_device.cuh); such a variant is built into its own object
+directory and written to --out (load it with CPAB_B200_LIB=PATH).
 
 The library is written next to the Python package
 (fg-cpab_b200/cpab/libcpab_b200.so) so that it ships with the source tree.
@@ -42,34 +46,42 @@ def _mtime(path):
     return os.path.getmtime(path) if os.path.exists(path) else -1.0
 
 
-def build(force=False, verbose=False, extra_flags=()):
-    """Compile (if stale) and link the library; returns its path."""
-    os.makedirs(OBJ_DIR, exist_ok=True)
+def build(force=False, verbose=False, extra_flags=(), out=None):
+    """Compile (if stale) and link the library; returns its path.  With
+    `out`, objects go to a directory of their own beside it."""
+    lib_path = LIB_PATH if out is None else os.path.abspath(out)
+    obj_dir = OBJ_DIR if out is None else lib_path + ".objs"
+    os.makedirs(obj_dir, exist_ok=True)
     nvcc = _nvcc()
     deps = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "cpab_b200.h")]
     dep_time = max(_mtime(p) for p in deps)
     objs = []
     for src in SOURCES:
         src_path = os.path.join(CSRC, src)
-        obj = os.path.join(OBJ_DIR, src.replace(".cu", ".o"))
+        obj = os.path.join(obj_dir, src.replace(".cu", ".o"))
         objs.append(obj)
         if force or _mtime(obj) < max(_mtime(src_path), dep_time):
             cmd = [nvcc, *NVCC_FLAGS, *extra_flags, "-I", INCLUDE, "-c", src_path, "-o", obj]
             if verbose:
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
-    if force or _mtime(LIB_PATH) < max(_mtime(o) for o in objs):
-        tmp = LIB_PATH + ".tmp"
+    if force or _mtime(lib_path) < max(_mtime(o) for o in objs):
+        tmp = lib_path + ".tmp"
         cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
                "-cudart", "static", "-Xcompiler", "-fPIC", *objs, "-o", tmp]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-        os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+        os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":
-    path = build(force="--force" in sys.argv, verbose=True,
-                 extra_flags=["-Xptxas", "-v"] if "--ptxas-v" in sys.argv else [])
+    args = sys.argv[1:]
+    defines = [a for a in args if a.startswith("-D")]
+    out = args[args.index("--out") + 1] if "--out" in args else None
+    if defines and out is None:
+        sys.exit("a -D variant needs --out PATH (the default library keeps the default choices)")
+    flags = (["-Xptxas", "-v"] if "--ptxas-v" in args else []) + defines
+    path = build(force="--force" in args, verbose=True, extra_flags=flags, out=out)
     print(path)

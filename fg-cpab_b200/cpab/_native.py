@@ -12,7 +12,10 @@ import os
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcpab_b200.so")
+# The library built next to this file; CPAB_B200_LIB names another build of
+# the same ABI (e.g. one with other compile-time kernel choices).
+LIB_PATH = os.environ.get("CPAB_B200_LIB") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "libcpab_b200.so")
 
 _c_int, _c_i64, _c_float, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 

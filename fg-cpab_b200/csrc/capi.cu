@@ -50,17 +50,6 @@ int64_t cell_count(int ndim, const int32_t *nc) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-cpab::Tess make_tess(int ndim, const int32_t *nc) {
-  cpab::Tess t;
-  t.nx = nc[0];
-  t.ny = ndim > 1 ? nc[1] : 1;
-  t.nz = ndim > 2 ? nc[2] : 1;
-  t.fx = (float)t.nx;
-  t.fy = (float)t.ny;
-  t.fz = (float)t.nz;
-  return t;
-}
-
 // Checks shared by forward and backward; fills the geometry part of `a`.
 int check_integrate(const char *fn, int ndim, const int32_t *nc, const float *points, int64_t nP,
                     int points_batched, const float *As, int n_theta, int nstepsolver,
@@ -87,7 +76,7 @@ int check_integrate(const char *fn, int ndim, const int32_t *nc, const float *po
   if (!aligned16(As)) return fail(CPAB_ERR_ARG, "%s: As must be 16-byte aligned", fn);
   a = cpab::IntegrateArgs{};
   a.ndim = ndim;
-  a.tess = make_tess(ndim, nc);
+  a.tess = cpab::make_tess(ndim, nc);
   a.nC = (int)nC;
   a.points = points;
   a.nP = nP;
@@ -266,7 +255,7 @@ int cpab_b200_order_points(int ndim, const int32_t *nc, const float *points, int
   if (nP > INT32_MAX) return fail(CPAB_ERR_SIZE, "order_points: more than 2^31-1 points");
   if (nP > 0 && n_sets > 0 && (points == nullptr || counts_scratch == nullptr || order == nullptr))
     return fail(CPAB_ERR_ARG, "order_points: null pointer");
-  return cuda_status(cpab::launch_order_points(ndim, make_tess(ndim, nc), points, nP, n_sets,
+  return cuda_status(cpab::launch_order_points(ndim, cpab::make_tess(ndim, nc), points, nP, n_sets,
                                                (int)nC, counts_scratch, order, stream),
                      "order_points");
 }
@@ -277,7 +266,7 @@ int cpab_b200_cell_index(int ndim, const int32_t *nc, const float *points, int64
   if (cell_count(ndim, nc) <= 0) return fail(CPAB_ERR_ARG, "cell_index: tessellation sizes must be in [1, 2^20]");
   if (n < 0) return fail(CPAB_ERR_ARG, "cell_index: negative number of points");
   if (n > 0 && (points == nullptr || cells == nullptr)) return fail(CPAB_ERR_ARG, "cell_index: null pointer");
-  return cuda_status(cpab::launch_cell_index(ndim, make_tess(ndim, nc), points, n, cells, stream),
+  return cuda_status(cpab::launch_cell_index(ndim, cpab::make_tess(ndim, nc), points, n, cells, stream),
                      "cell_index");
 }
 

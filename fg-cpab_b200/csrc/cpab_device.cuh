@@ -33,7 +33,26 @@ template <int ND> struct Dim {
 struct Tess {
   int nx, ny, nz;
   float fx, fy, fz;    // (float)n*
+  // Cell-index offsets that undo the 0x4B000000 bias of floor results read
+  // from float bit patterns (floor_nonneg): 2D -4 * 0x4B000000 * (1 + nx),
+  // 3D -5 * 0x4B000000 * (1 + nx + nx * ny), both modulo 2^32.
+  unsigned c2, c3;
 };
+
+// Tessellation geometry of an ndim tessellation with nc[k] cells per axis.
+inline Tess make_tess(int ndim, const int *nc) {
+  Tess t;
+  t.nx = nc[0];
+  t.ny = ndim > 1 ? nc[1] : 1;
+  t.nz = ndim > 2 ? nc[2] : 1;
+  t.fx = (float)t.nx;
+  t.fy = (float)t.ny;
+  t.fz = (float)t.nz;
+  const unsigned k = 0x4B000000u, nx = (unsigned)t.nx, ny = (unsigned)t.ny;
+  t.c2 = 0u - 4u * k * (1u + nx);
+  t.c3 = 0u - 5u * k * (1u + nx + nx * ny);
+  return t;
+}
 
 // floor(v) for 0 <= v < 2^22, as float and int, without conversion units:
 // v + 2^23 rounded toward -inf is 2^23 + floor(v) exactly.
@@ -102,11 +121,11 @@ __device__ __forceinline__ int cell_of(const Tess &t, float px, float py) {
   const float2 k23 = make_float2(8388608.0f, 8388608.0f);
   const float2 r = __fadd2_rd(__fmul2_rn(p, n), k23);
   const float2 l = __ffma2_rn(p, n, __ffma2_rn(r, make_float2(-1.0f, -1.0f), k23));
-  const int ix = __float_as_int(r.x) - 0x4B000000;
-  const int iy = __float_as_int(r.y) - 0x4B000000;
+  // r's bit patterns are 0x4B000000 + floor; t.c2 folds the bias out of the index
   const int upper_left = l.x < l.y;            // above the main diagonal
   const int upper_right = (1.0f - l.x) < l.y;  // above the anti-diagonal
-  return ((ix + iy * t.nx) << 2) + ((upper_left * 3) ^ upper_right);
+  const unsigned sq = __float_as_uint(r.x) + __float_as_uint(r.y) * (unsigned)t.nx;
+  return (int)((sq << 2) + t.c2) + ((upper_left * 3) ^ upper_right);
 }
 
 // 3D: five tetrahedra per cube (central one = 0), cube parity flips the
@@ -156,38 +175,45 @@ static __device__ __noinline__ int cell_of_3d_outside(int nx, int ny, int nz, fl
                      fminf(fmaxf(py, 0.0f), 1.0f) * fy, fminf(fmaxf(pz, 0.0f), 1.0f) * fz);
 }
 
-// Tetrahedron of cube (i, j, k) holding local coordinates (x, y, z) in [0, 1).
-__device__ __forceinline__ int tet_from_local(int nx, int ny, int i, int j, int k, float x,
-                                              float y, float z) {
-  const int c = 5 * (i + nx * (j + ny * k));
-  if ((i ^ j ^ k) & 1) {
-    const float x0 = x;
-    x = y;
-    y = 1.0f - x0;
-  }
-  if (-x - y + z >= 0.0f) return c + 1;
-  if (x + y + z - 2.0f >= 0.0f) return c + 2;
-  if (-x + y - z >= 0.0f) return c + 3;
-  if (x - y - z >= 0.0f) return c + 4;
-  return c;
-}
-
 __device__ __forceinline__ int cell_of(const Tess &t, float px, float py, float pz) {
-  // In [0, 1) the reference's clamps are identities, the corner rule does not
+  // In [+0, 1) the reference's clamps are identities, the corner rule does not
   // apply, and p * n rounds below n, so floor(p * n) <= n - 1 needs no clamp;
-  // everything else (including coordinates exactly 1) takes the general path.
-  if (px >= 0.0f && px < 1.0f && py >= 0.0f && py < 1.0f && pz >= 0.0f && pz < 1.0f) {
+  // everything else (including coordinates exactly 1, and -0, which the
+  // general path places identically) takes the general path.  As unsigned
+  // integers, the bit patterns of exactly the floats in [+0, 1) lie below
+  // that of 1.0f (negatives and NaN have larger patterns).
+  const unsigned hi = max(max(__float_as_uint(px), __float_as_uint(py)), __float_as_uint(pz));
+  if (hi < 0x3F800000u) {
     // floor_nonneg of x and y together (paired instructions, same roundings):
     // r = 2^23 + floor(s), floor = r - 2^23, and s - floor is exact.
     const float2 sxy = __fmul2_rn(make_float2(px, py), make_float2(t.fx, t.fy));
     const float2 r = __fadd2_rd(sxy, make_float2(8388608.0f, 8388608.0f));
     const float2 fxy = __fadd2_rn(r, make_float2(-8388608.0f, -8388608.0f));
     const float2 lxy = __ffma2_rn(fxy, make_float2(-1.0f, -1.0f), sxy);
-    int k;
     const float sz = pz * t.fz;
-    const float fk = floor_nonneg(sz, k);
-    return tet_from_local(t.nx, t.ny, __float_as_int(r.x) - 0x4B000000,
-                          __float_as_int(r.y) - 0x4B000000, k, lxy.x, lxy.y, sz - fk);
+    const float rz = __fadd_rd(sz, 8388608.0f);
+    const float z = sz - (rz - 8388608.0f);
+    // The bit patterns of r are 0x4B000000 + floor: the cube index comes from
+    // them directly (t.c3 folds the offsets), and so does its parity
+    // (0x4B000000 is even).
+    // (Unsigned: the intermediate products wrap modulo 2^32, the sum does not.)
+    const unsigned bx = __float_as_uint(r.x), by = __float_as_uint(r.y), bz = __float_as_uint(rz);
+    const int c = (int)(5u * (bx + (unsigned)t.nx * (by + (unsigned)t.ny * bz)) + t.c3);
+    float x = lxy.x, y = lxy.y;
+    if ((bx ^ by ^ bz) & 1) {  // odd cubes: rotate the local frame by 90 degrees
+      const float x0 = x;
+      x = y;
+      y = 1.0f - x0;
+    }
+    // The reference's four plane sums, from shared partial sums with the same
+    // roundings: -x - y = -(x + y) and x - y = -(-x + y) exactly, so
+    // x - y - z >= 0  <=>  (-x + y) + z <= 0.
+    const float a = x + y, b = -x + y;
+    int tet = (b + z <= 0.0f) ? 4 : 0;
+    tet = (b - z >= 0.0f) ? 3 : tet;
+    tet = ((a + z) - 2.0f >= 0.0f) ? 2 : tet;
+    tet = (-a + z >= 0.0f) ? 1 : tet;
+    return c + tet;
   }
   return cell_of_3d_outside(t.nx, t.ny, t.nz, px, py, pz);
 }
@@ -485,27 +511,138 @@ __device__ __forceinline__ void flush_smem(float *__restrict__ s_mom, int c, flo
   }
 }
 
-// Flush one cell's partial moments into the global moment table with vector
-// reductions (red.global.add.v4/v2.f32, resolved in L2; fire and forget):
-// P/4 or P/2 instructions per flush.  A shared-memory table would cost far
-// more here: fp32 atomics on shared memory are compare-and-swap loops, and the
-// lanes of a warp (processing points sorted by cell) usually hit the same
-// cell, so those loops retry once per lane.  g_mom must be 16-byte aligned
-// when P % 4 == 0 (3D rows of 12 floats), else 8-byte aligned.
+// Moment flush scheme, fixed at compile time (-DCPAB_MOMENT_FLUSH=n):
+//   0  every flushing lane adds its run straight into the global table with
+//      vector reductions (red.global.add.v4/v2.f32, resolved in L2; fire and
+//      forget): P/4 or P/2 instructions per flush;
+//   1  warp-aggregated: the flushing lanes are grouped by cell
+//      (__match_any_sync); a group that occupies a contiguous run of lanes is
+//      summed into its first lane by a segmented shuffle reduction (log2 of
+//      the longest run levels), which alone issues the reductions; lanes of
+//      scattered groups reduce on their own;
+//   2  warp-aggregated as the reference does it (cpab/core/cpab_ops_2d.cu:6-59):
+//      the lowest lane of each cell group gathers the others' moments one lane
+//      at a time by shuffles, then issues the reductions.
+// 0 is the default: aggregation trades a few L2 reductions for tens of
+// shuffle instructions per flush in a kernel bound by instruction issue.
+#ifndef CPAB_MOMENT_FLUSH
+#define CPAB_MOMENT_FLUSH 0
+#endif
+
+// Add one cell's moments v into the global table row c (vector reductions).
+// g_mom must be 16-byte aligned when P % 4 == 0 (3D rows of 12 floats), else
+// 8-byte aligned.
 template <int P>
-__device__ __forceinline__ void flush_moments(float *__restrict__ g_mom, int c, float (&mo)[P]) {
+__device__ __forceinline__ void red_row(float *__restrict__ g_mom, int c, const float (&v)[P]) {
   if constexpr (P % 4 == 0) {
     float4 *dst = reinterpret_cast<float4 *>(g_mom + (int64_t)c * P);
 #pragma unroll
     for (int k = 0; k < P / 4; ++k)
-      atomicAdd(dst + k, make_float4(mo[4 * k], mo[4 * k + 1], mo[4 * k + 2], mo[4 * k + 3]));
+      atomicAdd(dst + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
   } else {
     float2 *dst = reinterpret_cast<float2 *>(g_mom + (int64_t)c * P);
 #pragma unroll
-    for (int k = 0; k < P / 2; ++k) atomicAdd(dst + k, make_float2(mo[2 * k], mo[2 * k + 1]));
+    for (int k = 0; k < P / 2; ++k) atomicAdd(dst + k, make_float2(v[2 * k], v[2 * k + 1]));
   }
+}
+
+// Warp-aggregated red_row over the active lanes: lanes adding to the same cell
+// (__match_any_sync) that occupy a contiguous run of lanes are summed into the
+// run's first lane by a segmented shuffle reduction (log2 of the longest run
+// levels), which alone issues the reductions; lanes of scattered groups add
+// their own rows.  The summation order of a cell's contributions changes, not
+// the set.
+template <int P>
+__device__ __forceinline__ void red_row_warp(float *__restrict__ g_mom, int c,
+                                             const float (&mo)[P]) {
+  const unsigned act = __activemask();
+  const unsigned grp = __match_any_sync(act, c);
+  const int lane = threadIdx.x & 31;
+  const int lo = __ffs(grp) - 1, hi = 31 - __clz(grp);
+  // the group is the lanes lo..hi exactly (2u << 31 wraps to 0: all 32 lanes)
+  const bool run = (grp >> lo) == (2u << (hi - lo)) - 1u;
+  const int len = run ? hi - lo + 1 : 1;
+  const int longest = __reduce_max_sync(act, len);
+  if (longest == 1) {
+    red_row<P>(g_mom, c, mo);
+    return;
+  }
+  // Segmented suffix sums: after the level of offset `off`, lane i holds the
+  // sum over lanes i..min(i + 2 off - 1, hi) of its run.  Source lanes past
+  // the run's end (possibly inactive) are read but not used.
+  float v[P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) v[k] = mo[k];
+  for (int off = 1; off < longest; off <<= 1) {
+    const bool take = run && lane + off <= hi;
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const float o = __shfl_down_sync(act, v[k], off);
+      if (take) v[k] += o;
+    }
+  }
+  if (!run) red_row<P>(g_mom, c, mo);
+  else if (lane == lo) red_row<P>(g_mom, c, v);
+}
+
+// Flush one cell's partial moments mo into the global moment table and clear
+// them.  A shared-memory table would cost more than any scheme below: fp32
+// atomics on shared memory are compare-and-swap loops, and the lanes of a warp
+// (processing points sorted by cell) usually hit the same cell, so those loops
+// retry once per lane.  Called by the lanes whose cell changed (a divergent
+// branch): the warp-aggregated schemes group whichever lanes are active.
+template <int P>
+__device__ __forceinline__ void flush_moments(float *__restrict__ g_mom, int c, float (&mo)[P]) {
+#if CPAB_MOMENT_FLUSH == 0
+  red_row<P>(g_mom, c, mo);
+#elif CPAB_MOMENT_FLUSH == 1
+  red_row_warp<P>(g_mom, c, mo);
+#else
+  const unsigned act = __activemask();
+  const unsigned grp = __match_any_sync(act, c);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(grp) - 1;
+  if (grp == (1u << lane)) {
+    red_row<P>(g_mom, c, mo);
+  } else {
+    float s[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) s[k] = 0.0f;
+    for (unsigned peers = grp; peers != 0u; peers &= peers - 1u) {
+      const int src = __ffs(peers) - 1;
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const float o = __shfl_sync(grp, mo[k], src);
+        if (lane == leader) s[k] += o;
+      }
+    }
+    if (lane == leader) red_row<P>(g_mom, c, s);
+  }
+#endif
 #pragma unroll
   for (int k = 0; k < P; ++k) mo[k] = 0.0f;
+}
+
+// The last flush of a point's moments, at its initial cell.  The lanes of a
+// warp arrive together (converged, after the same number of steps) and, with
+// the points sorted by initial cell, mostly share that cell: their reductions
+// would all hit one address and serialize in L2, so they are aggregated over
+// the warp first.  Mid-trajectory flushes are rare (about one lane in a
+// hundred per step), divergent and spread over cells, so they stay per lane.
+// CPAB_FINAL_FLUSH_WARP=0 turns the aggregation off (for measurements).
+#ifndef CPAB_FINAL_FLUSH_WARP
+#define CPAB_FINAL_FLUSH_WARP 1
+#endif
+template <int P>
+__device__ __forceinline__ void flush_moments_final(float *__restrict__ g_mom, int c,
+                                                    float (&mo)[P]) {
+#if CPAB_FINAL_FLUSH_WARP && CPAB_MOMENT_FLUSH == 0
+  red_row_warp<P>(g_mom, c, mo);
+#pragma unroll
+  for (int k = 0; k < P; ++k) mo[k] = 0.0f;
+#else
+  flush_moments<P>(g_mom, c, mo);
+#endif
 }
 
 }  // namespace cpab

@@ -354,8 +354,17 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_mesh(IntegrateArgs a, M
 // (a warp's 32 entries of one step are 64 contiguous bytes), instead of in
 // each thread's local memory, whose ~200 bytes per thread across ~150k
 // resident threads overflow L1 into L2 and DRAM.
+// NT: the block size the kernel is launched with (a compile-time constant, so
+// that the per-thread slots of the shared-memory record are addressed with
+// immediate offsets).  AGG_FINAL: aggregate each point's last moment flush
+// over the warp (flush_moments_final).  Measured on one B200 (backward, CUDA
+// events): 2D bench workload 370 -> 362 us; the fused transform_data
+// backwards got slower (3D 2796 -> 2874 us, dense 2D 1591 -> 1639 us: the
+// dense 2D meshgrid is processed in output order, and a 3D flush is a small
+// share of its much longer steps), as did the 3D chain (6373 -> 6423 us), so
+// only the 2D transform_grid kernels aggregate.
 template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT, bool CHAIN,
-          class Src>
+          int NT, bool AGG_FINAL, class Src>
 __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   constexpr int S = kSegSteps;
@@ -414,15 +423,15 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     float ck_local[kCkSmem ? 1 : kMaxSegs][ND];
     float *s_ck = reinterpret_cast<float *>(
                       reinterpret_cast<char *>(s_cl - threadIdx.x) +
-                      (((size_t)a.T * blockDim.x * sizeof(CellT) + 15) & ~(size_t)15)) +
+                      (((size_t)a.T * NT * sizeof(CellT) + 15) & ~(size_t)15)) +
                   threadIdx.x;
     auto ck = [&](int seg, int k) -> float & {
-      if constexpr (kCkSmem) return s_ck[(seg * ND + k) * blockDim.x];
+      if constexpr (kCkSmem) return s_ck[(seg * ND + k) * NT];
       else return ck_local[seg][k];
     };
     CellT cl_local[(ADAPT || CL_SMEM) ? 1 : kMaxSteps];
     auto cl = [&](int step) -> CellT & {
-      if constexpr (CL_SMEM) return s_cl[step * blockDim.x];
+      if constexpr (CL_SMEM) return s_cl[step * NT];
       else return cl_local[step];
     };
     auto phase1 = [&](int seg, auto tail) {
@@ -490,7 +499,13 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     };
     if (rem) phase2(nfull, std::true_type{});
     for (int seg = nfull - 1; seg >= 0; --seg) phase2(seg, std::false_type{});
-    if (prev >= 0) flush(prev, mo);
+    // The last run ends at the point's initial cell, which the warp's lanes
+    // (sorted by initial cell) reach together and usually share.
+    if (prev >= 0) {
+      if constexpr (M_SMEM) flush_smem<P>(s_mom, prev, mo);
+      else if constexpr (AGG_FINAL) flush_moments_final<P>(gm, prev, mo);
+      else flush_moments<P>(gm, prev, mo);
+    }
     }
     src.grad(slot, i, lam);
   }
@@ -508,15 +523,16 @@ template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename C
           bool CHAIN = false, bool WIDE = false>
 __global__ void __launch_bounds__(BwdShape<ND, WIDE>::kThreads, BwdShape<ND, WIDE>::kMinBlocks)
     k_backward(IntegrateArgs a) {
-  backward_body<ND, ADAPT, A_SMEM, M_SMEM, CL_SMEM, CellT, CHAIN>(a, PointSrc<ND>(a, blockIdx.y));
+  backward_body<ND, ADAPT, A_SMEM, M_SMEM, CL_SMEM, CellT, CHAIN, BwdShape<ND, WIDE>::kThreads,
+                ND == 2>(a, PointSrc<ND>(a, blockIdx.y));
 }
 
 // Fused transform_data backward; GD: also the data gradient.
 template <int ND, bool ADAPT, bool A_SMEM, bool CL_SMEM, typename CellT, bool GD>
 __global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
     k_backward_mesh(IntegrateArgs a, MeshArgs m) {
-  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT, false>(a,
-                                                                MeshSrc<ND, GD>(a, m, blockIdx.y));
+  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT, false, BwdShape<ND>::kThreads, false>(
+      a, MeshSrc<ND, GD>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------

@@ -34,6 +34,23 @@ def test_clock_sampler_child_process(tmp_path, monkeypatch):
     assert c.proc.returncode == 0
 
 
+def test_clock_sampler_pauses_between_timed_regions(tmp_path, monkeypatch):
+    """Sampling covers several timed regions: start, pause, start again, stop."""
+    (tmp_path / "pynvml.py").write_text(FAKE_NVML)
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    c = bench.Clocks(0)
+    c.start()
+    time.sleep(0.02)
+    c.pause()
+    assert c.proc is not None
+    time.sleep(0.02)
+    c.start()
+    time.sleep(0.02)
+    r = c.stop()
+    assert r is not None and r["samples"] >= 4 and r["sm_mhz"] == 1800
+    assert c.proc.returncode == 0
+
+
 def test_clock_sampler_without_nvml_reports_nothing(tmp_path, monkeypatch):
     (tmp_path / "pynvml.py").write_text("raise ImportError('no NVML here')\n")
     monkeypatch.setenv("PYTHONPATH", str(tmp_path))
