@@ -443,7 +443,8 @@ def graph_replay(step, resident, C, flush, steps, warmup, clocks=None):
 
 # Native calls of the library timed per phase (CUDA events on the stream each
 # is enqueued on) and the kernels each launches.
-KERNELS_PER_CALL = {"build_A": 1, "order_points": 3, "project": 1, "interpolate": 1,
+KERNELS_PER_CALL = {"build_A": 1, "build_A_tt": 1, "order_points": 3, "project": 1,
+                    "project_tt": 1, "interpolate": 1,
                     "interpolate_backward": 1, "expm": 1, "forward": 1, "backward": 1,
                     "transform_data": 1, "transform_data_backward": 1, "forward_chain": 1,
                     "backward_chain": 1}
@@ -757,8 +758,9 @@ def run_ours(args, rank, world, local):
     if world == 1 and default and not args.no_ref_kernels:
         ref_kernels = ref_gpu_kernels(C, host, args.steps, args.warmup, flush)
         if ref_kernels is not None:
-            ours = {k: phases.get(k, 0.0) for k in ("build_A", "order_points", "forward",
-                                                    "backward", "project")}
+            ours = {k: phases.get(k, 0.0) for k in ("build_A", "build_A_tt", "order_points",
+                                                    "forward", "backward", "project",
+                                                    "project_tt") if k in phases}
             ours["fwd_grad_ms"] = sum(ours.values())
             ref_kernels = {
                 "what": "the reference's own CUDA kernels (cpab_ops_2d.cu, unmodified, sm_100a) "

@@ -32,6 +32,8 @@ _SIGNATURES = {
     "cpab_b200_order_points_static": [_c_int, _p, _p, _c_i64, _c_int, _p, _p],
     "cpab_b200_cell_index": [_c_int, _p, _p, _c_i64, _p, _p],
     "cpab_b200_project": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
+    "cpab_b200_build_A_tt": [_c_int, _c_i64, _c_i64, _c_int, _p, _p, _p, _p, _c_float, _p, _p, _p],
+    "cpab_b200_project_tt": [_c_i64, _c_i64, _c_int, _p, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p],
     "cpab_b200_interpolate_backward": [_c_int, _p, _c_int, _c_int, _p, _p, _p, _p, _p, _p, _p],
     "cpab_b200_forward_chain": [_c_int, _p, _p, _c_i64, _c_int, _p, _p, _p, _c_int, _c_int,
@@ -167,6 +169,19 @@ def build_A(ndim, nC, basis, theta, dT=None):
     return As, trels
 
 
+def build_A_tt(ndim, nC, basis, theta_t, n_theta, dT=None):
+    """build_A with theta given transposed, theta_t [d, n_theta]."""
+    _require(theta_t, "theta_t")
+    As = torch.empty((n_theta, nC, ndim, ndim + 1), device=theta_t.device, dtype=torch.float32)
+    trels = torch.empty_like(As) if dT is not None else None
+    with _on(theta_t.device):
+        _check(lib().cpab_b200_build_A_tt(
+            ndim, nC, basis.d, n_theta, _ptr(basis.rowptr), _ptr(basis.colidx), _ptr(basis.vals),
+            _ptr(theta_t), float(dT) if dT is not None else 0.0, _ptr(As), _ptr(trels),
+            _stream(theta_t.device)))
+    return As, trels
+
+
 def order_points(nc, points, batched):
     """Processing order of the points sorted by initial cell: int32
     [n_sets, nP] (n_sets = batch when batched, else 1)."""
@@ -250,6 +265,17 @@ def project(basis, moments):
         _check(lib().cpab_b200_project(
             basis.d, D, n_theta, _ptr(basis.t_rowptr), _ptr(basis.t_colidx), _ptr(basis.t_vals),
             _ptr(moments), _ptr(out), _stream(moments.device)))
+    return out
+
+
+def project_tt(basis, moments_t, n_theta):
+    """project with the moments given transposed, moments_t [D, n_theta]."""
+    _require(moments_t, "moments_t")
+    out = torch.empty((n_theta, basis.d), device=moments_t.device, dtype=torch.float32)
+    with _on(moments_t.device):
+        _check(lib().cpab_b200_project_tt(
+            basis.d, moments_t.shape[0], n_theta, _ptr(basis.t_rowptr), _ptr(basis.t_colidx),
+            _ptr(basis.t_vals), _ptr(moments_t), _ptr(out), _stream(moments_t.device)))
     return out
 
 

@@ -10,7 +10,7 @@ the composed autograd graph does.  Differentiable in theta and data.
 import torch
 
 from .. import _native
-from .transformer import _nc, device_basis
+from .transformer import _nc, build_A, device_basis, project
 
 
 def mesh_axes(params, outsize, device):
@@ -69,7 +69,7 @@ class _TransformData(torch.autograd.Function):
         T = int(params.nstepsolver)
         adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
         basis = device_basis(params, theta.device)
-        As, trels = _native.build_A(nd, int(params.nC), basis, theta.contiguous(), 1.0 / T)
+        As, trels = build_A(nd, int(params.nC), basis, theta.contiguous(), 1.0 / T)
         axes, order = _mesh(params, outsize, theta.device)
         data_c = data.contiguous()
         out, grid_t = _native.transform_data(nd, _nc(params), outsize, axes, trels, As, T,
@@ -90,6 +90,6 @@ class _TransformData(torch.autograd.Function):
         moments, gd = _native.transform_data_backward(
             params.ndim, _nc(params), ctx.outsize, axes, As, ctx.T, ctx.adaptive, data, grid_t,
             grad.contiguous(), want_data, ctx.order)
-        grad_theta = (_native.project(device_basis(params, As.device), moments)
+        grad_theta = (project(device_basis(params, As.device), moments)
                       if want_theta else None)
         return gd, grad_theta, None, None

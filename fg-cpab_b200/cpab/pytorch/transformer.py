@@ -20,7 +20,10 @@ from .. import _native
 
 @dataclass
 class DeviceBasis:
-    """CSR copies of B (D x d) and B^T (d x D) on one device, fp32 values."""
+    """CSR copies of B (D x d) and B^T (d x D) on one device, fp32 values.
+    ``dense``: more than 4 nonzeros per row of B on average (bases without the
+    zero-boundary constraint), whose A-build and projection run on
+    transposed operands (build_A / project below)."""
     d: int
     D: int
     rowptr: torch.Tensor
@@ -29,6 +32,7 @@ class DeviceBasis:
     t_rowptr: torch.Tensor
     t_colidx: torch.Tensor
     t_vals: torch.Tensor
+    dense: bool = False
 
 
 def _csr_arrays(M, device):
@@ -52,9 +56,28 @@ def device_basis(params, device):
         B = params.basis
         r, c, v = _csr_arrays(B, device)
         tr, tc, tv = _csr_arrays(B.T, device)
-        hit = DeviceBasis(int(B.shape[1]), int(B.shape[0]), r, c, v, tr, tc, tv)
+        hit = DeviceBasis(int(B.shape[1]), int(B.shape[0]), r, c, v, tr, tc, tv,
+                          dense=int(B.nnz) > 4 * int(B.shape[0]))
         cache[key] = hit
     return hit
+
+
+def build_A(ndim, nC, basis, theta, dT=None):
+    """As (and Trels when dT is given) for theta [n, d].  A general basis
+    spreads every row and column over the whole domain, so its products
+    gather scattered entries; there theta goes in transposed, which makes the
+    entries of all transformations at one basis column one contiguous load."""
+    if basis.dense:
+        return _native.build_A_tt(ndim, nC, basis, theta.t().contiguous(), theta.shape[0], dT)
+    return _native.build_A(ndim, nC, basis, theta, dT)
+
+
+def project(basis, moments):
+    """dtheta [n, d] = B^T vec(moments[n]) (moments transposed for general bases)."""
+    if basis.dense:
+        n = moments.shape[0]
+        return _native.project_tt(basis, moments.reshape(n, -1).t().contiguous(), n)
+    return _native.project(basis, moments)
 
 
 def _get_sparse_basis(params, device, dtype=torch.float32):
@@ -173,7 +196,7 @@ class _CPABFunction(torch.autograd.Function):
         T = int(params.nstepsolver)
         adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
         dT = None if nd == 1 else 1.0 / T
-        As, trels = _native.build_A(nd, int(params.nC), basis, theta_c, dT)
+        As, trels = build_A(nd, int(params.nC), basis, theta_c, dT)
         order = _order(params, points_c, batched)
         out = _native.forward(nd, _nc(params), points_c, batched, trels, As, T, adaptive, order)
         ctx.params = params
@@ -199,7 +222,7 @@ class _CPABFunction(torch.autograd.Function):
             grad_points = grad_points.sum(dim=0)
         grad_theta = None
         if ctx.needs_input_grad[1]:
-            grad_theta = _native.project(device_basis(params, As.device), moments)
+            grad_theta = project(device_basis(params, As.device), moments)
             if ctx.group is not None:
                 torch.distributed.all_reduce(grad_theta, group=ctx.group)
         return grad_points, grad_theta, None, None, None
@@ -226,7 +249,7 @@ class _ChainFunction(torch.autograd.Function):
         T = int(params.nstepsolver)
         adaptive = int(bool(getattr(params, "adaptive_substeps", False)))
         points_c = points.contiguous()
-        As, trels = _native.build_A(nd, int(params.nC), basis,
+        As, trels = build_A(nd, int(params.nC), basis,
                                     theta_stages.reshape(K * nb, d).contiguous(), 1.0 / T)
         order = _order(params, points_c, batched)
         out, sp = _native.forward_chain(nd, _nc(params), points_c, batched, trels, As, K, T,
@@ -249,6 +272,6 @@ class _ChainFunction(torch.autograd.Function):
             grad_points = grad_points.sum(dim=0)
         grad_theta = None
         if ctx.needs_input_grad[1]:
-            grad_theta = _native.project(device_basis(params, As.device), moments)
+            grad_theta = project(device_basis(params, As.device), moments)
             grad_theta = grad_theta.reshape(ctx.K, -1, grad_theta.shape[-1])
         return grad_points, grad_theta, None, None

@@ -5,7 +5,7 @@
 // These are small sparse contractions (a handful of nonzeros per row for
 // zero-boundary bases, dozens for general ones) -- gathers, not GEMMs -- so
 // they run on the SIMT pipes, one warp per cell (A-build) or per basis column
-// (projection) with the nonzeros split over the lanes.
+// (projection) with the lanes over the transformations.
 #include <cuda_runtime.h>
 
 #include "launch.h"
@@ -227,34 +227,44 @@ __global__ void k_expm(const float *__restrict__ As, int64_t n, float dT, float 
   for (int k = 0; k < P; ++k) trels[i * P + k] = r[k];
 }
 
-// Dot products of CSR row [k0, k1) with up to TC vectors x + u * stride
-// (u < nt), split over the 32 lanes of a warp: lane l sums products k0 + l,
-// k0 + l + 32, ... of every vector with an fmaf chain, and an xor butterfly
-// adds the lane partials; every lane returns all sums.  The index and value
-// of a nonzero are loaded once for the TC vectors, and the TC gathers and
-// chains are independent, so a warp keeps TC loads in flight instead of one.
-// (The per-vector order is fixed; the CPU oracle restates it.)
-constexpr int kDotChunk = 8;
+// Rows of a CSR matrix times up to 32 vectors at once, lanes over the vectors:
+// lane u of a warp sums row r of M times x[t0 + u] (x + (t0 + u) * stride)
+// with one sequential fmaf chain over the row's nonzeros -- the summation
+// order the CPU oracle restates.  The gathers x[t][col] of a row are staged
+// through shared memory 32 nonzeros at a time: lanes over nonzeros load a
+// vector's entries (the column indices of a row are sorted and clustered, so
+// these loads coalesce), store them transposed with a padded stride (33:
+// conflict-free both ways), then each lane reads its own vector's column.
+// A nonzero's value and column are loaded once for all vectors.
+constexpr int kStage = 32;
+constexpr int kStagePad = 33;
+constexpr int kWarpsPerBlock = 8;  // kThreads / 32
 
-template <int TC>
-__device__ __forceinline__ void warp_dots(const int32_t *__restrict__ colidx,
-                                          const float *__restrict__ vals, int k0, int k1,
-                                          const float *__restrict__ x, int64_t stride, int nt,
-                                          float (&out)[TC]) {
-#pragma unroll
-  for (int u = 0; u < TC; ++u) out[u] = 0.0f;
-  for (int k = k0 + (threadIdx.x & 31); k < k1; k += 32) {
-    const float v = __ldg(vals + k);
-    const float *xc = x + __ldg(colidx + k);
-#pragma unroll
-    for (int u = 0; u < TC; ++u)
-      if (u < nt) out[u] = fmaf(v, __ldg(xc + u * stride), out[u]);
+struct WarpStage {
+  float x[kStage * kStagePad];
+  float v[kStage];
+};
+
+__device__ __forceinline__ float row_times_lane_vector(const int32_t *__restrict__ colidx,
+                                                       const float *__restrict__ vals, int k0,
+                                                       int k1, const float *__restrict__ x,
+                                                       int64_t stride, int nt,
+                                                       WarpStage &st) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.0f;
+  for (int kc = k0; kc < k1; kc += kStage) {
+    const int n = min(kStage, k1 - kc);
+    __syncwarp();
+    if (lane < n) {
+      const int col = __ldg(colidx + kc + lane);
+      st.v[lane] = __ldg(vals + kc + lane);
+      const float *xc = x + col;
+      for (int u = 0; u < nt; ++u) st.x[lane * kStagePad + u] = __ldg(xc + u * stride);
+    }
+    __syncwarp();
+    for (int k = 0; k < n; ++k) acc = fmaf(st.v[k], st.x[k * kStagePad + lane], acc);
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-    for (int u = 0; u < TC; ++u) out[u] += __shfl_xor_sync(0xffffffffu, out[u], off);
-  }
+  return acc;
 }
 
 // A = B theta (and Trels = expm(A dT) when trels != NULL), in one of two
@@ -263,10 +273,11 @@ __device__ __forceinline__ void warp_dots(const int32_t *__restrict__ colidx,
 //   * sparse B (at most 4 nonzeros per row on average; zero-boundary bases
 //     have <= 4 in every row): one thread per (transformation, cell), each row
 //     summed with a sequential fmaf chain;
-//   * otherwise one warp per cell: each row's nonzeros split over the lanes
-//     (warp_dots), lane j keeping transformation t0 + j's entries, then each
-//     lane computes the exponential, 32 transformations wide.
-// The grid covers nC warps; the sparse mapping strides over nC * n_theta.
+//   * otherwise one warp per cell, lanes over transformations (32 at a time),
+//     each row through row_times_lane_vector; lane u then computes
+//     transformation t0 + u's exponential.
+// Both sum every entry with the same sequential chain.  The grid covers nC
+// warps; the sparse mapping strides over nC * n_theta.
 template <int ND>
 __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_theta,
                                                  const int32_t *__restrict__ rowptr,
@@ -303,38 +314,26 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
     }
     return;
   }
+  __shared__ WarpStage stage[kWarpsPerBlock];
+  WarpStage &st = stage[threadIdx.x >> 5];
   const int64_t c = gtid >> 5;
   const int lane = threadIdx.x & 31;
   if (c >= nC) return;  // whole warps exit together
-  int k0[P], k1[P];
-#pragma unroll
-  for (int r = 0; r < P; ++r) {
-    k0[r] = __ldg(rowptr + c * P + r);
-    k1[r] = __ldg(rowptr + c * P + r + 1);
-  }
   for (int t0 = 0; t0 < n_theta; t0 += 32) {
-    float mine[P];  // entries of transformation t0 + lane
-#pragma unroll
-    for (int r = 0; r < P; ++r) mine[r] = 0.0f;
     const int tn = min(32, n_theta - t0);
-    for (int j0 = 0; j0 < tn; j0 += kDotChunk) {
-      const float *th = theta + (int64_t)(t0 + j0) * d;
+    const float *th = theta + (int64_t)t0 * d;
+    float a[P];
 #pragma unroll
-      for (int r = 0; r < P; ++r) {
-        float sums[kDotChunk];
-        warp_dots<kDotChunk>(colidx, vals, k0[r], k1[r], th, d, tn - j0, sums);
-#pragma unroll
-        for (int u = 0; u < kDotChunk; ++u)
-          if (lane == j0 + u) mine[r] = sums[u];
-      }
-    }
+    for (int r = 0; r < P; ++r)
+      a[r] = row_times_lane_vector(colidx, vals, __ldg(rowptr + c * P + r),
+                                   __ldg(rowptr + c * P + r + 1), th, d, tn, st);
     if (lane < tn) {
       const int64_t base = ((int64_t)(t0 + lane) * nC + c) * P;
 #pragma unroll
-      for (int r = 0; r < P; ++r) As[base + r] = mine[r];
+      for (int r = 0; r < P; ++r) As[base + r] = a[r];
       if (trels != nullptr) {
         float e[P];
-        expm_cell<ND>(mine, dT, e);
+        expm_cell<ND>(a, dT, e);
 #pragma unroll
         for (int r = 0; r < P; ++r) trels[base + r] = e[r];
       }
@@ -342,26 +341,127 @@ __global__ void __launch_bounds__(256) k_build_A(int64_t nC, int64_t d, int n_th
   }
 }
 
-// dtheta[t, j] = sum over row j of B^T of vals * moments[t, col].  One warp
-// per basis column j (warp_dots; clustered column indices let the moment
-// gathers share sectors).  Columns have 16 to 80 nonzeros for zero-boundary
-// bases and up to ~1,700 for general ones.
-__global__ void __launch_bounds__(256) k_project(int64_t d, int64_t D, int n_theta,
-                                                 const int32_t *__restrict__ rowptr,
-                                                 const int32_t *__restrict__ colidx,
-                                                 const float *__restrict__ vals,
-                                                 const float *__restrict__ moments,
-                                                 float *__restrict__ dtheta) {
-  const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  if (j >= d) return;
-  const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
-  const int lane = threadIdx.x & 31;
-  for (int t0 = 0; t0 < n_theta; t0 += kDotChunk) {
-    float sums[kDotChunk];
-    warp_dots<kDotChunk>(colidx, vals, k0, k1, moments + (int64_t)t0 * D, D, n_theta - t0, sums);
+// The same products with the vectors given transposed, xt[col * nt + t]
+// (theta^T [d, n_theta] or moments^T [D, n_theta]): a nonzero's entries of
+// all vectors are then one contiguous row, so lanes over the vectors read it
+// as one coalesced load instead of n_theta scattered ones.  This is what
+// makes general (dense) bases cheap: their rows and columns spread over the
+// whole domain, so the untransposed gathers hit a different sector for every
+// vector.  Sequential fmaf chain per row (the oracle's order).
+// xl points at this lane's vector in column 0 (xt + t); nt is the row length.
+__device__ __forceinline__ float row_times_lane_vector_t(const int32_t *__restrict__ colidx,
+                                                         const float *__restrict__ vals, int k0,
+                                                         int k1, const float *__restrict__ xl,
+                                                         int nt) {
+  float acc = 0.0f;
+  int k = k0;
+  // four loads in flight per chain step; the chain itself stays sequential
+  for (; k + 4 <= k1; k += 4) {
+    const int c0 = __ldg(colidx + k), c1 = __ldg(colidx + k + 1);
+    const int c2 = __ldg(colidx + k + 2), c3 = __ldg(colidx + k + 3);
+    const float x0 = __ldg(xl + (int64_t)c0 * nt), x1 = __ldg(xl + (int64_t)c1 * nt);
+    const float x2 = __ldg(xl + (int64_t)c2 * nt), x3 = __ldg(xl + (int64_t)c3 * nt);
+    acc = fmaf(__ldg(vals + k), x0, acc);
+    acc = fmaf(__ldg(vals + k + 1), x1, acc);
+    acc = fmaf(__ldg(vals + k + 2), x2, acc);
+    acc = fmaf(__ldg(vals + k + 3), x3, acc);
+  }
+  for (; k < k1; ++k) acc = fmaf(__ldg(vals + k), __ldg(xl + (int64_t)__ldg(colidx + k) * nt), acc);
+  return acc;
+}
+
+// k_build_A with theta given transposed (theta_t [d, n_theta]): one block per
+// cell, one warp per row of the cell (so the longest dependent chain is one
+// row, not the cell's ppc rows in turn), lanes over the transformations, 32
+// at a time (in the last group, lanes past n_theta repeat the last
+// transformation, in bounds, and store nothing).  Warp 0 then takes the
+// cell's entries from shared memory and computes the exponentials.
+template <int ND>
+__global__ void __launch_bounds__(32 * Dim<ND>::kPpc) k_build_A_tt(
+    int64_t nC, int n_theta, const int32_t *__restrict__ rowptr,
+    const int32_t *__restrict__ colidx, const float *__restrict__ vals,
+    const float *__restrict__ theta_t, float dT, float *__restrict__ As,
+    float *__restrict__ trels) {
+  constexpr int P = Dim<ND>::kPpc;
+  __shared__ float s_a[P][32];
+  const int64_t c = blockIdx.x;
+  const int r = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = __ldg(rowptr + c * P + r), k1 = __ldg(rowptr + c * P + r + 1);
+  for (int t0 = 0; t0 < n_theta; t0 += 32) {
+    const int t = min(t0 + lane, n_theta - 1);
+    s_a[r][lane] = row_times_lane_vector_t(colidx, vals, k0, k1, theta_t + t, n_theta);
+    __syncthreads();
+    if (r == 0 && t0 + lane < n_theta) {
+      float a[P];
 #pragma unroll
-    for (int u = 0; u < kDotChunk; ++u)
-      if (lane == u && t0 + u < n_theta) dtheta[(int64_t)(t0 + u) * d + j] = sums[u];
+      for (int q = 0; q < P; ++q) a[q] = s_a[q][lane];
+      const int64_t base = ((int64_t)t * nC + c) * P;
+#pragma unroll
+      for (int q = 0; q < P; ++q) As[base + q] = a[q];
+      if (trels != nullptr) {
+        float e[P];
+        expm_cell<ND>(a, dT, e);
+#pragma unroll
+        for (int q = 0; q < P; ++q) trels[base + q] = e[q];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// dtheta[t, j] = sum over row j of B^T (basis column j) of vals * moments[t,
+// col].  One block per basis column, lanes over the transformations.  Columns
+// have 16 to 80 nonzeros for zero-boundary bases and up to ~1,700 for general
+// ones, so a column is cut into chunks of kProjChunk nonzeros that the
+// block's warps sum concurrently (an fmaf chain each); warp 0 then adds the
+// chunk sums left to right -- the order the CPU oracle restates.  Chunk sums
+// pass through shared memory kProjGroup chunks at a time.  TT: moments given
+// transposed ([D, n_theta], one coalesced load per nonzero; for general
+// bases, whose columns spread over the whole domain); otherwise [n_theta, D],
+// gathered through row_times_lane_vector's staging.
+constexpr int kProjWarps = 8;
+constexpr int kProjChunk = 32;  // = kStage
+constexpr int kProjGroup = 64;
+
+template <bool TT>
+__global__ void __launch_bounds__(32 * kProjWarps) k_project(int64_t d, int64_t D, int n_theta,
+                                                             const int32_t *__restrict__ rowptr,
+                                                             const int32_t *__restrict__ colidx,
+                                                             const float *__restrict__ vals,
+                                                             const float *__restrict__ m,
+                                                             float *__restrict__ dtheta) {
+  __shared__ float s_part[kProjGroup][32];
+  const int64_t j = blockIdx.x;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = __ldg(rowptr + j), k1 = __ldg(rowptr + j + 1);
+  const int nch = (k1 - k0 + kProjChunk - 1) / kProjChunk;
+  for (int t0 = 0; t0 < n_theta; t0 += 32) {
+    const int tn = min(32, n_theta - t0);
+    const int t = min(t0 + lane, n_theta - 1);
+    float total = 0.0f;  // warp 0: the column's running sum for transformation t
+    for (int g0 = 0; g0 < nch; g0 += kProjGroup) {
+      const int gn = min(kProjGroup, nch - g0);
+      for (int i = w; i < gn; i += kProjWarps) {
+        const int kc = k0 + (g0 + i) * kProjChunk, ke = min(kc + kProjChunk, k1);
+        float sum;
+        if constexpr (TT) {
+          sum = row_times_lane_vector_t(colidx, vals, kc, ke, m + t, n_theta);
+        } else {
+          __shared__ WarpStage stage[kProjWarps];
+          sum = row_times_lane_vector(colidx, vals, kc, ke, m + (int64_t)t0 * D, D, tn, stage[w]);
+        }
+        s_part[i][lane] = sum;
+      }
+      __syncthreads();
+      if (w == 0) {
+        for (int i = 0; i < gn; ++i) {
+          const float part = s_part[i][lane];
+          total = g0 + i == 0 ? part : total + part;
+        }
+      }
+      __syncthreads();
+    }
+    if (w == 0 && lane < tn) dtheta[(int64_t)(t0 + lane) * d + j] = total;
   }
 }
 
@@ -404,13 +504,46 @@ cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const i
   return cudaGetLastError();
 }
 
+cudaError_t launch_build_A_tt(int ndim, int64_t nC, int n_theta, const int32_t *rowptr,
+                              const int32_t *colidx, const float *vals, const float *theta_t,
+                              float dT, float *As, float *trels, cudaStream_t s) {
+  if (nC * n_theta == 0) return cudaSuccess;
+  if (nC > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)nC;  // one block per cell, one warp per row
+  switch (ndim) {
+    case 1:
+      k_build_A_tt<1><<<grid, 32 * Dim<1>::kPpc, 0, s>>>(nC, n_theta, rowptr, colidx, vals,
+                                                         theta_t, dT, As, trels);
+      break;
+    case 2:
+      k_build_A_tt<2><<<grid, 32 * Dim<2>::kPpc, 0, s>>>(nC, n_theta, rowptr, colidx, vals,
+                                                         theta_t, dT, As, trels);
+      break;
+    default:
+      k_build_A_tt<3><<<grid, 32 * Dim<3>::kPpc, 0, s>>>(nC, n_theta, rowptr, colidx, vals,
+                                                         theta_t, dT, As, trels);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_project_tt(int64_t d, int n_theta, const int32_t *rowptr,
+                              const int32_t *colidx, const float *vals, const float *moments_t,
+                              float *dtheta, cudaStream_t s) {
+  if (d * n_theta == 0) return cudaSuccess;
+  if (d > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  k_project<true><<<(unsigned)d, 32 * kProjWarps, 0, s>>>(d, 0, n_theta, rowptr, colidx, vals,
+                                                          moments_t, dtheta);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_project(int64_t d, int64_t D, int n_theta, const int32_t *rowptr,
                            const int32_t *colidx, const float *vals, const float *moments,
                            float *dtheta, cudaStream_t s) {
   if (d * n_theta == 0) return cudaSuccess;
-  const int64_t n = d * 32;  // one warp per basis column
-  k_project<<<blocks_for(n), kThreads, 0, s>>>(d, D, n_theta, rowptr, colidx, vals, moments,
-                                               dtheta);
+  if (d > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  k_project<false><<<(unsigned)d, 32 * kProjWarps, 0, s>>>(d, D, n_theta, rowptr, colidx, vals,
+                                                           moments, dtheta);
   return cudaGetLastError();
 }
 

@@ -129,6 +129,20 @@ int cpab_b200_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_
                      "build_A");
 }
 
+int cpab_b200_build_A_tt(int ndim, int64_t nC, int64_t d, int n_theta, const int32_t *B_rowptr,
+                         const int32_t *B_colidx, const float *B_vals, const float *theta_t,
+                         float dT, float *As, float *trels, cpab_stream_t stream) {
+  if (ndim < 1 || ndim > 3) return fail(CPAB_ERR_ARG, "build_A_tt: ndim must be 1, 2 or 3");
+  if (nC < 0 || d < 0 || n_theta < 0) return fail(CPAB_ERR_ARG, "build_A_tt: negative size");
+  if (nC * n_theta > 0 &&
+      (B_rowptr == nullptr || As == nullptr || (d > 0 && (theta_t == nullptr || B_colidx == nullptr ||
+                                                           B_vals == nullptr))))
+    return fail(CPAB_ERR_ARG, "build_A_tt: null pointer");
+  return cuda_status(cpab::launch_build_A_tt(ndim, nC, n_theta, B_rowptr, B_colidx, B_vals,
+                                             theta_t, dT, As, trels, stream),
+                     "build_A_tt");
+}
+
 int cpab_b200_forward_1d_closed_form(const float *points, int64_t nP, int points_batched,
                                      const int32_t *order, const float *As, int n_theta, int ncx,
                                      float *out, cpab_stream_t stream) {
@@ -281,6 +295,19 @@ int cpab_b200_project(int64_t d, int64_t D, int n_theta, const int32_t *Bt_rowpt
   return cuda_status(
       cpab::launch_project(d, D, n_theta, Bt_rowptr, Bt_colidx, Bt_vals, moments, dtheta, stream),
       "project");
+}
+
+int cpab_b200_project_tt(int64_t d, int64_t D, int n_theta, const int32_t *Bt_rowptr,
+                         const int32_t *Bt_colidx, const float *Bt_vals, const float *moments_t,
+                         float *dtheta, cpab_stream_t stream) {
+  if (d < 0 || D < 0 || n_theta < 0) return fail(CPAB_ERR_ARG, "project_tt: negative size");
+  if (d * n_theta > 0 && (Bt_rowptr == nullptr || dtheta == nullptr ||
+                          (D > 0 && (moments_t == nullptr || Bt_colidx == nullptr ||
+                                     Bt_vals == nullptr))))
+    return fail(CPAB_ERR_ARG, "project_tt: null pointer");
+  return cuda_status(cpab::launch_project_tt(d, n_theta, Bt_rowptr, Bt_colidx, Bt_vals, moments_t,
+                                             dtheta, stream),
+                     "project_tt");
 }
 
 }  // extern "C"

@@ -527,12 +527,13 @@ __global__ void __launch_bounds__(BwdShape<ND, WIDE>::kThreads, BwdShape<ND, WID
                 ND == 2>(a, PointSrc<ND>(a, blockIdx.y));
 }
 
-// Fused transform_data backward; GD: also the data gradient.
-template <int ND, bool ADAPT, bool A_SMEM, bool CL_SMEM, typename CellT, bool GD>
-__global__ void __launch_bounds__(BwdShape<ND>::kThreads, BwdShape<ND>::kMinBlocks)
+// Fused transform_data backward; GD: also the data gradient.  WIDE as for
+// k_backward: one 1024-thread block per SM holding one copy of the table.
+template <int ND, bool ADAPT, bool A_SMEM, bool CL_SMEM, typename CellT, bool GD, bool WIDE = false>
+__global__ void __launch_bounds__(BwdShape<ND, WIDE>::kThreads, BwdShape<ND, WIDE>::kMinBlocks)
     k_backward_mesh(IntegrateArgs a, MeshArgs m) {
-  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT, false, BwdShape<ND>::kThreads, false>(
-      a, MeshSrc<ND, GD>(a, m, blockIdx.y));
+  backward_body<ND, ADAPT, A_SMEM, false, CL_SMEM, CellT, false, BwdShape<ND, WIDE>::kThreads,
+                false>(a, MeshSrc<ND, GD>(a, m, blockIdx.y));
 }
 
 // ---------------------------------------------------------------------------
@@ -812,6 +813,16 @@ cudaError_t mesh_backward_cells(const IntegrateArgs &a, const MeshArgs &m, cudaS
   constexpr int kT = BwdShape<ND>::kThreads;
   constexpr bool kCl = !ADAPT && sizeof(CellT) == 2;
   const size_t cl = kCl ? cell_record_bytes<ND, CellT>(kT, a.T) : 0;
+  if constexpr (ND == 2 && kCl) {
+    // 2D: the table and the cell record of 1024 threads in one block when
+    // they fit (the 30 x 30 table beside a 512-thread record does not fit
+    // two blocks' budget, and the record would go to local memory).
+    constexpr int kW = BwdShape<ND, true>::kThreads;
+    const size_t cl_wide = (size_t)kW * a.T * sizeof(CellT);
+    if (tab + cl > kBwdSmemBudget && tab + cl_wide <= kBwdWideSmemBudget)
+      return launch_wave_args(k_backward_mesh<ND, ADAPT, true, true, CellT, GD, true>, kW,
+                              tab + cl_wide, a, m, s);
+  }
   if (tab <= kBwdSmemBudget) {
     if constexpr (kCl) {
       if (tab + cl <= kBwdSmemBudget)

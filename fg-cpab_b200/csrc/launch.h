@@ -68,6 +68,12 @@ cudaError_t launch_expm(int ndim, const float *As, int64_t n, float dT, float *t
 cudaError_t launch_build_A(int ndim, int64_t nC, int64_t d, int n_theta, const int32_t *rowptr,
                            const int32_t *colidx, const float *vals, const float *theta,
                            float dT, float *As, float *trels, cudaStream_t s);
+cudaError_t launch_build_A_tt(int ndim, int64_t nC, int n_theta, const int32_t *rowptr,
+                              const int32_t *colidx, const float *vals, const float *theta_t,
+                              float dT, float *As, float *trels, cudaStream_t s);
+cudaError_t launch_project_tt(int64_t d, int n_theta, const int32_t *rowptr,
+                              const int32_t *colidx, const float *vals, const float *moments_t,
+                              float *dtheta, cudaStream_t s);
 cudaError_t launch_project(int64_t d, int64_t D, int n_theta, const int32_t *rowptr,
                            const int32_t *colidx, const float *vals, const float *moments,
                            float *dtheta, cudaStream_t s);

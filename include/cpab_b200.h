@@ -133,6 +133,19 @@ int cpab_b200_backward(int ndim, const int32_t *nc, const float *points,
                        cpab_stream_t stream);
 
 /*
+ * cpab_b200_build_A with theta given transposed, theta_t [d, n_theta]
+ * (theta_t[k * n_theta + t] = theta[t, k]); same results.  For bases with
+ * many nonzeros per row (zero_boundary=False), where the row entries of all
+ * transformations are then one contiguous load each.  Replaces the same
+ * reference lines as cpab_b200_build_A (cpab/pytorch/transformer.py:84-88,
+ * :104-106); the transposed operand has no counterpart there.
+ */
+int cpab_b200_build_A_tt(int ndim, int64_t nC, int64_t d, int n_theta,
+                         const int32_t *B_rowptr, const int32_t *B_colidx,
+                         const float *B_vals, const float *theta_t, float dT,
+                         float *As, float *trels, cpab_stream_t stream);
+
+/*
  * order[s, :] = the points of set s (s < n_sets; points [n_sets, ndim, nP],
  * or [ndim, nP] with n_sets = 1) sorted by the cell that contains them
  * (counting sort; ties in arbitrary order).  Passing it to forward/backward
@@ -181,6 +194,17 @@ int cpab_b200_project(int64_t d, int64_t D, int n_theta,
                       const int32_t *Bt_rowptr, const int32_t *Bt_colidx,
                       const float *Bt_vals, const float *moments,
                       float *dtheta, cpab_stream_t stream);
+
+/*
+ * cpab_b200_project with the moments given transposed, moments_t [D, n_theta]
+ * (moments_t[i * n_theta + t] = moments[t, i]); same results.  For general
+ * (dense) bases, whose columns spread over the whole domain.  Replaces
+ * cpab/pytorch/transformer.py:165-166 like cpab_b200_project.
+ */
+int cpab_b200_project_tt(int64_t d, int64_t D, int n_theta,
+                         const int32_t *Bt_rowptr, const int32_t *Bt_colidx,
+                         const float *Bt_vals, const float *moments_t,
+                         float *dtheta, cpab_stream_t stream);
 
 /*
  * Linear / bilinear / trilinear resampling of data [n_batch, C, *in_size] at

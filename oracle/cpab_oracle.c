@@ -534,34 +534,31 @@ void oracle_midpoint_forward(int nd, const int32_t *nc, const float *pts, int64_
 /* out[t, r] = sum over row r of a CSR matrix of vals * x[t, col] in float32,
  * in the order the GPU kernels use (the reference computes these products with
  * torch.sparse.mm, cpab/pytorch/transformer.py:84 and :166, whose fp32 order
- * is the library's).  lanes = 1: one fmaf chain over the row (the sparse
- * mapping of k_build_A); lanes = 32: lane l accumulates nonzeros l, l+32, ...
- * with fmaf, then an xor butterfly with offsets 16, ..., 1 adds the partials
- * (lane 0's value is returned). */
-static float lane_order_dot(const int32_t *colidx, const float *vals, int32_t k0, int32_t k1,
-                            const float *x, int W) {
-  float lane[32];
-  for (int l = 0; l < W; ++l) {
+ * is the library's).  chunk = 0: one fmaf chain over the row (k_build_A);
+ * chunk = K: an fmaf chain over every K consecutive nonzeros, and the chunk
+ * sums added left to right (k_project, whose chunks are summed by different
+ * warps).  A row of at most K nonzeros gets the single chain either way. */
+static float chunked_dot(const int32_t *colidx, const float *vals, int32_t k0, int32_t k1,
+                         const float *x, int K) {
+  if (K <= 0) K = k1 - k0 > 0 ? k1 - k0 : 1;
+  float total = 0.0f;
+  for (int32_t kc = k0; kc < k1; kc += K) {
+    const int32_t ke = kc + K < k1 ? kc + K : k1;
     float s = 0.0f;
-    for (int32_t k = k0 + l; k < k1; k += W) s = fmaf(vals[k], x[colidx[k]], s);
-    lane[l] = s;
+    for (int32_t k = kc; k < ke; ++k) s = fmaf(vals[k], x[colidx[k]], s);
+    total = kc == k0 ? s : total + s;
   }
-  for (int off = W / 2; off > 0; off >>= 1) {
-    float next[32];
-    for (int l = 0; l < W; ++l) next[l] = lane[l] + lane[l ^ off];
-    memcpy(lane, next, sizeof(float) * W);
-  }
-  return lane[0];
+  return total;
 }
 
 void oracle_csr_matmul(int64_t rows, const int32_t *rowptr, const int32_t *colidx,
                        const float *vals, int n_rhs, const float *x, int64_t x_stride,
-                       float *out, int64_t out_stride, int lanes) {
+                       float *out, int64_t out_stride, int chunk) {
 #pragma omp parallel for collapse(2) schedule(static)
   for (int t = 0; t < n_rhs; ++t) {
     for (int64_t r = 0; r < rows; ++r) {
-      out[(int64_t)t * out_stride + r] = lane_order_dot(colidx, vals, rowptr[r], rowptr[r + 1],
-                                                        x + (int64_t)t * x_stride, lanes);
+      out[(int64_t)t * out_stride + r] = chunked_dot(colidx, vals, rowptr[r], rowptr[r + 1],
+                                                     x + (int64_t)t * x_stride, chunk);
     }
   }
 }

@@ -107,34 +107,39 @@ def _csr32(M):
             np.ascontiguousarray(M.data, np.float32))
 
 
-def csr_matmul(M, X, lanes=32):
+# Nonzeros per chunk of the projection's rows (k_project sums 32-nonzero
+# chunks on different warps and adds the chunk sums left to right).
+PROJECT_CHUNK = 32
+
+
+def csr_matmul(M, X, chunk=0):
     """(M @ X^T)^T for a sparse M [rows, cols] and X [n, cols] in fp32, summed
-    in the GPU kernels' order: lanes = 1, one fma chain per row; lanes = 32,
-    32 strided lane partials with fma, then an xor butterfly over the lanes."""
+    in the GPU kernels' order: chunk = 0, one fma chain per row; chunk = K, an
+    fma chain per K consecutive nonzeros of a row, chunk sums added left to
+    right."""
     X = _f32(X)
     rp, ci, v = _csr32(M)
     rows = M.shape[0]
     out = np.empty((X.shape[0], rows), dtype=np.float32)
     lib().oracle_csr_matmul(rows, _ptr(rp), _ptr(ci), _ptr(v), X.shape[0], _ptr(X), X.shape[1],
-                            _ptr(out), rows, lanes)
+                            _ptr(out), rows, int(chunk))
     return out
 
 
 def build_A(basis, theta, ndim):
-    """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T (fp32)."""
+    """As [n_theta, nC, ndim, ndim+1] = reshape(B theta^T)^T (fp32), every
+    entry one fma chain over its row of B (k_build_A's order in both of its
+    mappings)."""
     th = _f32(theta)
     nC = basis.shape[0] // (ndim * (ndim + 1))
-    # k_build_A's mapping: a chain per entry when B has <= 4 nonzeros per row
-    # on average, else rows split over a warp.
-    nnz = len(_csr32(basis)[1])
-    lanes = 1 if nnz <= 4 * basis.shape[0] else 32
-    return csr_matmul(basis, th, lanes).reshape(th.shape[0], nC, ndim, ndim + 1)
+    return csr_matmul(basis, th, 0).reshape(th.shape[0], nC, ndim, ndim + 1)
 
 
 def project(basis, moments):
-    """dtheta [n_theta, d] = B^T vec(moments) (fp32)."""
+    """dtheta [n_theta, d] = B^T vec(moments) (fp32), every entry summed in
+    32-nonzero chunks of its row of B^T (k_project's order)."""
     m = _f32(moments).reshape(moments.shape[0], -1)
-    return csr_matmul(basis.T, m)
+    return csr_matmul(basis.T, m, PROJECT_CHUNK)
 
 
 def integrate(nc, points, As, trels, nstepsolver=50, adaptive=False):

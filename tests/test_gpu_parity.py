@@ -152,3 +152,43 @@ def test_zero_theta_is_exact_identity():
         pts = torch.rand(len(nc), 10000, device=DEV)
         out = C.transform_grid(pts, C.identity(3))
         assert torch.equal(out, pts.expand(3, -1, -1))
+
+
+# (nc, zero_boundary, n_theta): sparse and general bases, fewer and more
+# transformations than a warp's 32 lanes.
+PRODUCT_CASES = [((30, 30), False, 32), ((30, 30), False, 40), ((5, 3), False, 7),
+                 ((20, 20), True, 16), ((6,), False, 33), ((4, 3, 2), False, 3),
+                 ((10, 10, 10), True, 4)]
+
+
+@pytest.mark.parametrize("case", PRODUCT_CASES,
+                         ids=["%s-zb%d-t%d" % ("x".join(map(str, c[0])), c[1], c[2])
+                              for c in PRODUCT_CASES])
+def test_basis_products_match_oracle_bit_for_bit(case):
+    """A = B theta and dtheta = B^T m, through both the plain entry points and
+    the transposed-operand ones (used for general bases): every entry is one
+    sequential fma chain over its row, as the oracle sums it, so all four
+    agree with the oracle exactly; both Trels are the same GPU expm of the
+    same A (against the oracle's libm-based expm within 1e-6, as above)."""
+    nc, zb, n_theta = case
+    C = cpab(nc, zb)
+    p, nd = C.params, len(nc)
+    th = rand_theta(n_theta, p.d, 11, 0.7)
+    th_d = torch.from_numpy(th).to(DEV)
+    basis = device_basis(p, th_d.device)
+    dT = None if nd == 1 else 1.0 / 50
+    ref_A = O.build_A(p.basis, th, nd)
+    A1, T1 = _native.build_A(nd, p.nC, basis, th_d, dT)
+    A2, T2 = _native.build_A_tt(nd, p.nC, basis, th_d.t().contiguous(), n_theta, dT)
+    np.testing.assert_array_equal(A1.cpu().numpy(), ref_A)
+    np.testing.assert_array_equal(A2.cpu().numpy(), ref_A)
+    if dT is not None:
+        np.testing.assert_array_equal(T1.cpu().numpy(), T2.cpu().numpy())
+        np.testing.assert_allclose(T1.cpu().numpy(), O.expm(ref_A, dT), rtol=1e-6, atol=1e-6)
+    mom = np.random.default_rng(12).standard_normal((n_theta, p.nC, nd * (nd + 1))).astype(np.float32)
+    mom_d = torch.from_numpy(mom).to(DEV)
+    ref_d = O.project(p.basis, mom)
+    d1 = _native.project(basis, mom_d)
+    d2 = _native.project_tt(basis, mom_d.reshape(n_theta, -1).t().contiguous(), n_theta)
+    np.testing.assert_array_equal(d1.cpu().numpy(), ref_d)
+    np.testing.assert_array_equal(d2.cpu().numpy(), ref_d)
