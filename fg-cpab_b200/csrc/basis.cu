@@ -355,16 +355,19 @@ __device__ __forceinline__ float row_times_lane_vector_t(const int32_t *__restri
                                                          int nt) {
   float acc = 0.0f;
   int k = k0;
-  // four loads in flight per chain step; the chain itself stays sequential
-  for (; k + 4 <= k1; k += 4) {
-    const int c0 = __ldg(colidx + k), c1 = __ldg(colidx + k + 1);
-    const int c2 = __ldg(colidx + k + 2), c3 = __ldg(colidx + k + 3);
-    const float x0 = __ldg(xl + (int64_t)c0 * nt), x1 = __ldg(xl + (int64_t)c1 * nt);
-    const float x2 = __ldg(xl + (int64_t)c2 * nt), x3 = __ldg(xl + (int64_t)c3 * nt);
-    acc = fmaf(__ldg(vals + k), x0, acc);
-    acc = fmaf(__ldg(vals + k + 1), x1, acc);
-    acc = fmaf(__ldg(vals + k + 2), x2, acc);
-    acc = fmaf(__ldg(vals + k + 3), x3, acc);
+  // eight nonzeros' loads in flight ahead of the (sequential) chain: the
+  // chain's length is what bounds these kernels, through load latency
+  for (; k + 8 <= k1; k += 8) {
+    int c[8];
+    float v[8], x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) c[u] = __ldg(colidx + k + u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __ldg(vals + k + u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = __ldg(xl + (int64_t)c[u] * nt);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = fmaf(v[u], x[u], acc);
   }
   for (; k < k1; ++k) acc = fmaf(__ldg(vals + k), __ldg(xl + (int64_t)__ldg(colidx + k) * nt), acc);
   return acc;
