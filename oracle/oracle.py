@@ -6,8 +6,9 @@ CPU-baseline legs of bench.py, as the checker -- never by the product.
   * integration / adjoint / expm / cell lookup: liboracle.so, the C
     restatement in cpab_oracle.c (cpab/core/cpab_ops_{1,2,3}d.cu);
   * A = B theta and dtheta = B^T m: fp32 CSR products summed in the GPU
-    kernels' fixed order (lane partials + xor butterfly), as torch.sparse.mm
-    computes them in cpab/pytorch/transformer.py:84-88, :165-166;
+    kernels' fixed order (one fma chain per row for A; 32-nonzero chunk sums
+    added left to right for dtheta), the products torch.sparse.mm computes
+    in cpab/pytorch/transformer.py:84-88, :165-166;
   * resampling: numpy float32 restatement of cpab/pytorch/interpolation.py:8-160
     (forward, op for op) and of the gradient its autograd graph produces.
 
