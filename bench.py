@@ -312,7 +312,7 @@ class Workload:
         self.scaling, self.parallelism = scaling, parallelism
 
 
-def make_workload(name, rank, world, dev):
+def make_workload(name, rank, world, dev, unfused=False):
     """Build (workload, host inputs, step function, pairs per step on this rank)."""
     from cpab import Cpab
     from cpab.distributed import allreduce_theta_grad, shard_points, transform_grid_sharded
@@ -363,6 +363,24 @@ def make_workload(name, rank, world, dev):
         host = {"theta": torch.randn(B, C.params.d, generator=gen(0)) * scale, "data": data,
                 "target": target}
         outsize = shape[1:]
+
+        if unfused:
+            # the reference's composition (cpab/cpab.py:306-308) through the
+            # same library: meshgrid, transform_grid, interpolate
+            del w.fused_data
+            w.desc += " (unfused: uniform_meshgrid + transform_grid + interpolate)"
+            # a fixed meshgrid keeps its sort order, as the fused path keeps
+            # its meshgrid's processing order
+            w.keep_order = True
+            grid = C.uniform_meshgrid(outsize, device=dev)
+
+            def step(x):
+                t = x["theta"].requires_grad_(True)
+                out = C.interpolate(x["data"], C.transform_grid(grid, t), outsize)
+                loss = F.mse_loss(out, x["target"])
+                loss.backward()
+                return loss, t.grad
+            return w, C, host, step, B * int(np.prod(outsize))
 
         def step(x):
             t = x["theta"].requires_grad_(True)
@@ -538,16 +556,21 @@ def profile_record():
 
 
 def breakdown(fn, steps, flush, world, timer):
-    """Per-phase ms of fn (every native call and allreduce bracketed by
-    events), from a pass of its own, so that the events' host time does not
-    enter the step times reported beside it."""
+    """(per-phase ms, kernels of this library per step) of fn: every native
+    call and allreduce bracketed by CUDA events, in a pass of its own so that
+    the events' host time does not enter the step times reported beside it.
+    The pass takes the Python autograd node, whose C ABI calls the timer
+    wraps; the C++ node (the default path) issues the same calls."""
+    from cpab import _ext
     rec = {}
     timer.rec, timer.only = rec, None
     n0 = timer.launches
-    timed_steps(fn, steps, flush, world)
+    with _ext.python_path():
+        timed_steps(fn, steps, flush, world)
     timer.rec = None
+    per_step = (timer.launches - n0) / steps
     timer.launches = n0
-    return phase_ms(rec, steps, world)
+    return phase_ms(rec, steps, world), per_step
 
 
 def strong_scaling(C, steps, warmup, flush, rank, world, timer):
@@ -587,7 +610,7 @@ def strong_scaling(C, steps, warmup, flush, rank, world, timer):
         torch.cuda.synchronize()
         ms = timed_steps(fn, steps, flush, world)
         out[name] = {"value": BATCH * N_POINTS / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
-                     "phase_ms": breakdown(fn, steps, flush, world, timer)}
+                     "phase_ms": breakdown(fn, steps, flush, world, timer)[0]}
     out["points_sharded"]["how"] = ("the 125,000 points split over the ranks, all 16 "
                                     "transformations on every rank, one dtheta allreduce")
     out["batch_sharded"]["how"] = ("all 125,000 points on every rank, %d of the 16 "
@@ -669,7 +692,7 @@ def run_ours(args, rank, world, local):
     # rank 0 samples the clocks; its sampler process starts now, long before
     # the timed steps, and idles until they begin
     clocks = Clocks(local) if rank == 0 else None
-    w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev)
+    w, C, host, step, pairs_rank = make_workload(args.config, rank, world, dev, args.unfused)
     default = args.config == "2d"
 
     fused = getattr(w, "fused_data", None) is not None
@@ -685,10 +708,13 @@ def run_ours(args, rank, world, local):
 
     from cpab.pytorch.transformer import clear_order_cache
 
+    keep_order = getattr(w, "keep_order", False)
+
     def dev_step():
         # Every step sorts its points again, as a step on a new batch would
         # (the library would otherwise keep the order of the unchanged points).
-        clear_order_cache(C.params)
+        if not keep_order:
+            clear_order_cache(C.params)
         return step(dict(resident, theta=resident["theta"].detach()))
 
     for _ in range(args.warmup):
@@ -697,19 +723,14 @@ def run_ours(args, rank, world, local):
 
     if clocks is not None:
         clocks.start()
-    # Events bracket the two integration kernels only (their mean launch time
-    # feeds the roofline); the other calls are counted.
-    rec = {}
-    timer.rec, timer.only = rec, set(names)
+    # The step as a user runs it: no events but the step's own.
     ms_step = timed_steps(dev_step, args.steps, flush, world)
-    timer.rec = None
-    launches = timer.launches
     if clocks is not None:
         clocks.pause()
-    kern = {k: max_over_ranks(sum(s.elapsed_time(e) for s, e in rec.get(n, [])) / args.steps,
-                              world)
-            for k, n in (("forward", names[0]), ("backward", names[1]))}
-    phases = breakdown(dev_step, args.steps, flush, world, timer)
+    # Per-call CUDA events (and the kernel count) from a pass of the same steps.
+    phases, launches_per_step = breakdown(dev_step, args.steps, flush, world, timer)
+    launches = int(round(launches_per_step * args.steps))
+    kern = {k: phases.get(n, 0.0) for k, n in (("forward", names[0]), ("backward", names[1]))}
     pairs_step = pairs_rank * world
     value = pairs_step / (ms_step * 1e-3)
 
@@ -806,7 +827,9 @@ def run_ours(args, rank, world, local):
             "workload": w.desc, "tess": w.tess, "batch": w.batch, "stages": w.stages,
             "nstepsolver": NSTEP, "global_batch": pairs_step, "parallelism": w.parallelism,
             "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20),
-            "point_order": MESH_ORDER_NOTE if fused else ORDER_NOTE}
+            "point_order": (MESH_ORDER_NOTE if fused else
+                            "fixed meshgrid: its sort order is computed once and kept"
+                            if keep_order else ORDER_NOTE)}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -825,8 +848,9 @@ def run_ours(args, rank, world, local):
             "kernel_ms": kern,
             "phase_ms": phases,
             "phase_note": "mean ms per step of each native call (and allreduce), CUDA events "
-                          "in a separate pass of the same steps; the remainder of a step is "
-                          "torch's loss kernels and host launch gaps",
+                          "in a separate pass of the same steps (kernel_ms and the roofline "
+                          "use these); the remainder of a step is torch's loss kernels and "
+                          "launch gaps",
             "graph_replay": None if graph_ms is None else {
                 "value": pairs_step / (graph_ms * 1e-3), "unit": UNIT, "ms_per_step": graph_ms,
                 "note": "the value step captured once in a CUDA graph and replayed; "
@@ -872,6 +896,9 @@ def main():
                     help="skip the strong-scaling figures of the N>1 default run")
     ap.add_argument("--no-ref-kernels", action="store_true",
                     help="skip timing the reference's own GPU kernels at N=1")
+    ap.add_argument("--unfused", action="store_true",
+                    help="dense2d / 3d: time the unfused composition (meshgrid, transform_grid, "
+                         "interpolate) instead of the fused transform_data kernels")
     ap.add_argument("--config", default="2d",
                     choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d"],
                     help="workload (default: BASELINE configs[1], 2D 20x20)")

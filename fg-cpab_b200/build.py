@@ -76,6 +76,43 @@ def build(force=False, verbose=False, extra_flags=(), out=None):
     return lib_path
 
 
+EXT_NAME = "_cpab_ext"
+EXT_PATH = os.path.join(OUT_DIR, EXT_NAME + ".so")
+EXT_SRC = os.path.join(CSRC, "torch_ext.cpp")
+
+
+def build_ext(force=False, verbose=False):
+    """Compile the C++ autograd node (csrc/torch_ext.cpp, host code only) into
+    cpab/_cpab_ext.so against this Python's torch, linked to libcpab_b200.so
+    (found next to it at run time).  Returns its path."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    lib = build(verbose=verbose)
+    if not (force or _mtime(EXT_PATH) < max(_mtime(EXT_SRC), _mtime(lib), _mtime(__file__),
+                                           _mtime(os.path.join(INCLUDE, "cpab_b200.h")))):
+        return EXT_PATH
+    cuda_home = cpp_extension.CUDA_HOME or "/usr/local/cuda"
+    incs = cpp_extension.include_paths() + [sysconfig.get_paths()["include"], INCLUDE,
+                                            os.path.join(cuda_home, "include")]
+    libdirs = cpp_extension.library_paths()
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = EXT_PATH + ".tmp"
+    cmd = (["g++", "-O2", "-std=c++17", "-fPIC", "-shared", EXT_SRC, "-o", tmp,
+            "-D_GLIBCXX_USE_CXX11_ABI=%d" % abi, "-DTORCH_EXTENSION_NAME=" + EXT_NAME,
+            "-DTORCH_API_INCLUDE_EXTENSION_H", "-Wno-deprecated-declarations"]
+           + ["-I" + i for i in incs] + ["-L" + d for d in libdirs]
+           + ["-L" + OUT_DIR, "-lcpab_b200", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+              "-ltorch_cuda", "-ltorch_python", "-Wl,-rpath,$ORIGIN"])
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, EXT_PATH)
+    return EXT_PATH
+
+
 if __name__ == "__main__":
     args = sys.argv[1:]
     defines = [a for a in args if a.startswith("-D")]
@@ -85,3 +122,5 @@ if __name__ == "__main__":
     flags = (["-Xptxas", "-v"] if "--ptxas-v" in args else []) + defines
     path = build(force="--force" in args, verbose=True, extra_flags=flags, out=out)
     print(path)
+    if out is None and "--no-ext" not in args:
+        print(build_ext(force="--force" in args, verbose=True))

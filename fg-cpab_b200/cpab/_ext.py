@@ -1,0 +1,47 @@
+"""Loader of _cpab_ext.so, the C++ autograd node of transform_grid
+(csrc/torch_ext.cpp, built by fg-cpab_b200/build.py next to this file).
+
+It computes exactly what _CPABFunction computes (the same C ABI calls with the
+same arguments) with far less host time per step.  transform_grid uses it
+when it is built and CPAB_B200_NO_EXT is not set; the Python node stays for
+point-sharded calls (whose backward allreduces dtheta) and otherwise.
+"""
+import importlib.machinery
+import importlib.util
+import os
+
+import torch  # noqa: F401  (libtorch must be loaded before the extension)
+
+import contextlib
+
+PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_cpab_ext.so")
+_mod = None
+_off = 0
+
+
+@contextlib.contextmanager
+def python_path():
+    """Within this context transform_grid takes the Python autograd node (the
+    benchmark's per-call instrumentation wraps that path's C ABI calls)."""
+    global _off
+    _off += 1
+    try:
+        yield
+    finally:
+        _off -= 1
+
+
+def module():
+    """The extension module, or None when it is not built or disabled."""
+    global _mod
+    if _off:
+        return None
+    if _mod is None:
+        if os.environ.get("CPAB_B200_NO_EXT") or not os.path.exists(PATH):
+            return None
+        loader = importlib.machinery.ExtensionFileLoader("_cpab_ext", PATH)
+        spec = importlib.util.spec_from_file_location("_cpab_ext", PATH, loader=loader)
+        mod = importlib.util.module_from_spec(spec)
+        loader.exec_module(mod)
+        _mod = mod
+    return _mod

@@ -13,7 +13,7 @@ replicated; outputs stay sharded.
 import torch
 import torch.distributed as dist
 
-from .pytorch.transformer import _CPABFunction
+from .pytorch.transformer import transform
 
 
 def shard_bounds(n_points, rank, world_size):
@@ -40,7 +40,7 @@ def transform_grid_sharded(cpab, grid_shard, theta, group=None, compute_points_g
         group = dist.group.WORLD
     if group is not None and dist.get_world_size(group) == 1:
         group = None
-    return _CPABFunction.apply(grid_shard, theta, cpab.params, compute_points_grad, group)
+    return transform(grid_shard, theta, cpab.params, compute_points_grad, group)
 
 
 def allreduce_theta_grad(theta, group=None):

@@ -22,12 +22,15 @@ def _mesh(params, outsize, device):
     """(axes, order) of the meshgrid of outsize, cached per params/device.
 
     order is the processing order of the output points, sorted by initial
-    cell, for 3D: 3D cell tables are read from global memory, so a warp that
-    starts inside one tetrahedron loads its rows once (the unsorted output
-    order crosses several cubes per warp and measured ~30% slower).  2D
-    tables are staged in shared memory and output order (coalesced writes)
-    is used.  A miss under CUDA graph capture is built inside the graph and
-    not cached (its contents exist only in the graph's replays).
+    cell: the lanes of a warp then start in one cell and mostly stay
+    together, so they take the same branches, read the same table rows
+    (broadcasts in 2D, where the table is in shared memory; one load in 3D,
+    where it is read from global memory) and flush moments to the same rows.
+    The output and the resample's gathers stay local (a cell is a patch of
+    neighbouring pixels).  Measured on one B200 against output order: 3D
+    config 5.55 -> 4.33 ms per step, dense 2D config 2.50 -> 2.32 ms.  A
+    miss under CUDA graph capture is built inside the graph and not cached
+    (its contents exist only in the graph's replays).
     """
     cache = params.__dict__.setdefault("_mesh_axes", {})
     key = (tuple(int(s) for s in outsize), str(device))
@@ -37,11 +40,9 @@ def _mesh(params, outsize, device):
         lin = [torch.linspace(params.domain_min[i], params.domain_max[i], int(n), device=device)
                for i, n in enumerate(outsize)]
         axes = torch.cat(lin).contiguous()
-        order = None
-        if params.ndim == 3:
-            mesh = torch.meshgrid(*lin, indexing="ij")  # output order: last axis fastest
-            pts = torch.stack([g.reshape(-1) for g in mesh]).contiguous()
-            order = _native.order_points(_nc(params), pts, False)[0].contiguous()
+        mesh = torch.meshgrid(*lin, indexing="ij")  # output order: last axis fastest
+        pts = torch.stack([g.reshape(-1) for g in mesh]).contiguous()
+        order = _native.order_points(_nc(params), pts, False)[0].contiguous()
         hit = (axes, order)
         if not capturing:
             cache[key] = hit

@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .. import _native
+from .. import _ext, _native
 
 
 @dataclass
@@ -33,6 +33,10 @@ class DeviceBasis:
     t_colidx: torch.Tensor
     t_vals: torch.Tensor
     dense: bool = False
+
+    @property
+    def tensors(self):
+        return [self.rowptr, self.colidx, self.vals, self.t_rowptr, self.t_colidx, self.t_vals]
 
 
 def _csr_arrays(M, device):
@@ -117,7 +121,33 @@ def CPAB_transformer(points, theta, params, compute_points_grad=False):
     assert points.is_cuda and theta.is_cuda, "Only GPU tensors supported"
     assert params.ndim in (1, 2, 3), "GPU transformer supports 1D, 2D, and 3D"
     assert type(compute_points_grad) == bool, "compute_points_grad must be bool"
-    return _CPABFunction.apply(points, theta, params, compute_points_grad, None)
+    return transform(points, theta, params, compute_points_grad, None)
+
+
+def transform(points, theta, params, compute_points_grad=False, group=None):
+    """The transform_grid autograd node: the C++ one (_cpab_ext) when it is
+    built, else _CPABFunction; a process group (backward allreduces dtheta)
+    always takes _CPABFunction.  Both issue the same C ABI calls."""
+    ext = _ext.module() if group is None else None
+    if ext is None:
+        return _CPABFunction.apply(points, theta, params, compute_points_grad, group)
+    batched, _ = _layout(points, theta, params)
+    if theta.dtype != torch.float32 or points.dtype != torch.float32:
+        raise TypeError("points and theta must be float32")
+    basis = device_basis(params, theta.device)
+    points_c = points.contiguous()
+    try:
+        return ext.transform(points_c, theta, basis.tensors, basis.d, basis.dense, _nc(params),
+                             int(params.nstepsolver),
+                             bool(getattr(params, "adaptive_substeps", False)),
+                             _order(params, points_c, batched), compute_points_grad, batched)
+    except RuntimeError as e:
+        # a failed C ABI call (the node's message starts with the library's
+        # name) raises the same error type as the Python path
+        first = str(e).split("\n", 1)[0]
+        if first.startswith("libcpab_b200: "):
+            raise _native.CpabNativeError(first[len("libcpab_b200: "):]) from None
+        raise
 
 
 def _layout(points, theta, params):

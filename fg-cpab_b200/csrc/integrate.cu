@@ -122,8 +122,9 @@ template <int ND> struct PointSrc {
 };
 
 // transform_data (2D/3D): the uniform meshgrid of out_size, output point o =
-// order[slot] (or slot: output order); forward writes the integrated grid (at
-// the slot: coalesced) and resamples every channel of data at it
+// order[slot] (the library passes the meshgrid sorted by initial cell; NULL:
+// output order); forward writes the integrated grid (at the slot: coalesced)
+// and resamples every channel of data at it
 // (cpab/cpab.py:306-308 = transform_grid then interpolate); backward forms the
 // upstream gradient from the resample gradient at the saved grid, as the
 // unfused autograd graph does (GD: also scatter grad_data).
@@ -359,10 +360,9 @@ __global__ void __launch_bounds__(kFwdThreads) k_forward_mesh(IntegrateArgs a, M
 // immediate offsets).  AGG_FINAL: aggregate each point's last moment flush
 // over the warp (flush_moments_final).  Measured on one B200 (backward, CUDA
 // events): 2D bench workload 370 -> 362 us; the fused transform_data
-// backwards got slower (3D 2796 -> 2874 us, dense 2D 1591 -> 1639 us: the
-// dense 2D meshgrid is processed in output order, and a 3D flush is a small
-// share of its much longer steps), as did the 3D chain (6373 -> 6423 us), so
-// only the 2D transform_grid kernels aggregate.
+// backwards got slower (3D 2796 -> 2874 us, where a flush is a small share of
+// the much longer steps; dense 2D 1484 -> 1519 us), as did the 3D chain
+// (6373 -> 6423 us), so only the 2D transform_grid kernels aggregate.
 template <int ND, bool ADAPT, bool A_SMEM, bool M_SMEM, bool CL_SMEM, typename CellT, bool CHAIN,
           int NT, bool AGG_FINAL, class Src>
 __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src &src) {

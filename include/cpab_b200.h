@@ -273,7 +273,8 @@ int cpab_b200_backward_chain(int ndim, const int32_t *nc, const float *points,
  * data is [n_theta, n_channels, *in_size], out [n_theta, n_channels,
  * *out_size] (P = prod(out_size) points, last axis fastest).  order (may be
  * NULL): a permutation of the P output indices giving the processing order,
- * e.g. cpab_b200_order_points of the meshgrid in output order; the kernel's
+ * e.g. cpab_b200_order_points applied to the meshgrid's points listed in
+ * output order (the cell-sorted order the Python package passes); the kernel's
  * thread slot s handles output point order[s].  grid_t receives the
  * integrated grid as [n_theta, ndim, P] indexed by slot, which the backward
  * (given the same order) needs.  Results equal the unfused composition of

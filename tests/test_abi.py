@@ -169,3 +169,14 @@ def test_misaligned_tables_rejected():
     assert L.cpab_b200_forward(2, NC2, P, 10, 0, None, odd, P, 1, 50, 0, P, None) == -1
     big = (ctypes.c_int32 * 2)((1 << 20) + 1, 2)
     assert L.cpab_b200_forward(2, big, P, 10, 0, None, P, P, 1, 50, 0, P, None) == -1
+
+
+def test_cpp_extension_loads_next_to_the_library():
+    """The C++ autograd node is built beside libcpab_b200.so and imports
+    without a GPU (it only links the library; no CUDA call at import)."""
+    from cpab import _ext
+    m = _ext.module()
+    assert m is not None and hasattr(m, "transform")
+    with _ext.python_path():
+        assert _ext.module() is None
+    assert _ext.module() is m
