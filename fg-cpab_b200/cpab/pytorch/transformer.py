@@ -124,11 +124,21 @@ def CPAB_transformer(points, theta, params, compute_points_grad=False):
     return transform(points, theta, params, compute_points_grad, None)
 
 
+def _allreduce_grad(group):
+    def hook(g):
+        g = g.contiguous().clone()
+        torch.distributed.all_reduce(g, group=group)
+        return g
+    return hook
+
+
 def transform(points, theta, params, compute_points_grad=False, group=None):
     """The transform_grid autograd node: the C++ one (_cpab_ext) when it is
-    built, else _CPABFunction; a process group (backward allreduces dtheta)
-    always takes _CPABFunction.  Both issue the same C ABI calls."""
-    ext = _ext.module() if group is None else None
+    built, else _CPABFunction; both issue the same C ABI calls.  With a
+    process group, dtheta is summed over the group once per backward: for the
+    C++ node by a gradient hook on an identity view of theta, so that exactly
+    this node's contribution is reduced (as _CPABFunction's backward does)."""
+    ext = _ext.module()
     if ext is None:
         return _CPABFunction.apply(points, theta, params, compute_points_grad, group)
     batched, _ = _layout(points, theta, params)
@@ -136,6 +146,9 @@ def transform(points, theta, params, compute_points_grad=False, group=None):
         raise TypeError("points and theta must be float32")
     basis = device_basis(params, theta.device)
     points_c = points.contiguous()
+    if group is not None and theta.requires_grad:
+        theta = theta.view_as(theta)
+        theta.register_hook(_allreduce_grad(group))
     try:
         return ext.transform(points_c, theta, basis.tensors, basis.d, basis.dense, _nc(params),
                              int(params.nstepsolver),

@@ -72,6 +72,22 @@ def _hook_sum(rank, world, port, q):
         q.put((rank, repr(e)))
 
 
+def _node_hook_sum(rank, world, port, q):
+    """The C++ transform node's sharded form: a hook on an identity view of
+    theta sums only the gradient that flows through the view."""
+    try:
+        _init(rank, world, port)
+        from cpab.pytorch.transformer import _allreduce_grad
+        theta = torch.zeros(4, 5, requires_grad=True)
+        view = theta.view_as(theta)
+        view.register_hook(_allreduce_grad(None))
+        ((view * (rank + 1)).sum() + (theta * 2.0).sum()).backward()
+        q.put((rank, theta.grad.numpy().copy()))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
 def _one_rank_leaves(rank, world, port, q):
     _init(rank, world, port, timeout_s=5)
     if rank == 1:
@@ -118,6 +134,13 @@ def test_theta_gradient_hook_sums_over_ranks():
     out = _run(_hook_sum)
     for r in (0, 1):
         np.testing.assert_allclose(out[r], np.full((4, 5), (1 + 2) + 2 * 2.0))
+
+
+def test_node_gradient_hook_sums_only_the_node_contribution():
+    out = _run(_node_hook_sum)
+    for r in (0, 1):
+        # the view's gradient (rank + 1) is summed over ranks, the rest is not
+        np.testing.assert_allclose(out[r], np.full((4, 5), (1 + 2) + 2.0))
 
 
 def test_rank_leaving_turns_into_an_error_not_a_hang():

@@ -62,3 +62,4 @@ def test_cpp_node_rejects_cpu_tensors_and_bad_shapes():
         CPAB_transformer(torch.rand(2, 100), th, C.params)
     with pytest.raises(ValueError):
         transform(torch.rand(3, 100, device="cuda"), th, C.params)
+
