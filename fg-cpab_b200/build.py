@@ -24,8 +24,8 @@ LIB_NAME = "libcpab_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 OBJ_DIR = os.path.join(HERE, "_build")
 
-SOURCES = ["integrate.cu", "basis.cu", "resample.cu", "capi.cu", "noalloc.cu"]
-HEADERS = ["cpab_device.cuh", "launch.h"]
+SOURCES = ["integrate.cu", "warp.cu", "basis.cu", "resample.cu", "capi.cu", "noalloc.cu"]
+HEADERS = ["cpab_device.cuh", "integrate_body.cuh", "launch.h", "resample_device.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -55,16 +55,23 @@ def build(force=False, verbose=False, extra_flags=(), out=None):
     nvcc = _nvcc()
     deps = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "cpab_b200.h")]
     dep_time = max(_mtime(p) for p in deps)
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         src_path = os.path.join(CSRC, src)
         obj = os.path.join(obj_dir, src.replace(".cu", ".o"))
         objs.append(obj)
         if force or _mtime(obj) < max(_mtime(src_path), dep_time):
-            cmd = [nvcc, *NVCC_FLAGS, *extra_flags, "-I", INCLUDE, "-c", src_path, "-o", obj]
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append([nvcc, *NVCC_FLAGS, *extra_flags, "-I", INCLUDE, "-c", src_path, "-o", obj])
+    # The translation units are independent: compile them side by side (the
+    # two integration units take most of the time).
+    procs = []
+    for cmd in cmds:
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append((cmd, subprocess.Popen(cmd)))
+    failed = [cmd for cmd, p in procs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     if force or _mtime(lib_path) < max(_mtime(o) for o in objs):
         tmp = lib_path + ".tmp"
         cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,10 +1,11 @@
-"""Loader of _cpab_ext.so, the C++ autograd node of transform_grid
-(csrc/torch_ext.cpp, built by fg-cpab_b200/build.py next to this file).
+"""Loader of _cpab_ext.so, the C++ autograd nodes of transform_grid and of
+the spatial-transformer warp (csrc/torch_ext.cpp, built by
+fg-cpab_b200/build.py next to this file).
 
-It computes exactly what _CPABFunction computes (the same C ABI calls with the
-same arguments) with far less host time per step.  transform_grid uses it
-when it is built and CPAB_B200_NO_EXT is not set; the Python node stays for
-point-sharded calls (whose backward allreduces dtheta) and otherwise.
+They compute exactly what the Python nodes (_CPABFunction, warp._Warp)
+compute -- the same C ABI calls with the same arguments -- with far less host
+time per step.  The package uses them when the extension is built and
+CPAB_B200_NO_EXT is not set; the Python nodes are the fallback otherwise.
 """
 import importlib.machinery
 import importlib.util
@@ -45,3 +46,17 @@ def module():
         loader.exec_module(mod)
         _mod = mod
     return _mod
+
+
+def call(fn, *args):
+    """fn(*args) of the extension; a failed C ABI call (the node's message
+    starts with the library's name) raises the same error type as the
+    Python path."""
+    from . import _native
+    try:
+        return fn(*args)
+    except RuntimeError as e:
+        first = str(e).split("\n", 1)[0]
+        if first.startswith("libcpab_b200: "):
+            raise _native.CpabNativeError(first[len("libcpab_b200: "):]) from None
+        raise

@@ -44,6 +44,10 @@ _SIGNATURES = {
                                  _c_int, _p, _p, _p, _p],
     "cpab_b200_transform_data_backward": [_c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int,
                                           _p, _c_int, _p, _p, _p, _p, _p, _p],
+    "cpab_b200_warp": [_c_int, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p,
+                       _c_int, _c_int, _p, _c_int, _p, _p, _p, _p],
+    "cpab_b200_warp_backward": [_c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p,
+                                _c_int, _c_int, _p, _c_int, _p, _p, _p, _p, _p, _p],
 }
 
 EXPORTS = tuple(_SIGNATURES) + ("cpab_b200_version", "cpab_b200_max_steps",
@@ -340,6 +344,61 @@ def transform_data_backward(ndim, nc, outsize, axes, As, nstepsolver, adaptive, 
             ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(As), n_theta,
             int(nstepsolver), int(adaptive), _ptr(data), C, _i64_array(data.shape[2:]),
             _ptr(grid_t), _ptr(grad_out), _ptr(moments), _ptr(gd), _stream(As.device)))
+    return moments, gd
+
+
+def _data_batched(data, n_theta):
+    """1 when data holds one image per transformation, 0 for one shared image."""
+    if data.shape[0] not in (1, n_theta):
+        raise ValueError("data must hold 1 or n_theta = %d images, got %d" % (n_theta, data.shape[0]))
+    return int(data.shape[0] == n_theta)
+
+
+def warp(ndim, nc, outsize, axes, trels, As, n_stages, nstepsolver, adaptive, data, padding,
+         order=None):
+    """Fused spatial-transformer warp of n_theta = As.shape[0] / n_stages
+    transformations; data is [n_theta, C, *in_size] or [1, C, *in_size]
+    (shared).  Returns (out [n_theta, C, *outsize], grid_t [n_theta, ndim, P],
+    stage_points [n_stages-1, n_theta, ndim, P] or None)."""
+    _require(data, "data")
+    _require(As, "As")
+    _require(trels, "Trels")
+    _require(axes, "mesh axes")
+    n_theta, C = As.shape[0] // n_stages, data.shape[1]
+    P = int(np_prod(outsize))
+    out = torch.empty((n_theta, C, *outsize), device=As.device, dtype=torch.float32)
+    grid_t = torch.empty((n_theta, ndim, P), device=As.device, dtype=torch.float32)
+    sp = (torch.empty((n_stages - 1, n_theta, ndim, P), device=As.device, dtype=torch.float32)
+          if n_stages > 1 else None)
+    batched = _data_batched(data, n_theta)
+    with _on(As.device):
+        _check(lib().cpab_b200_warp(
+            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(trels),
+            _ptr(As), n_stages, n_theta, int(nstepsolver), int(adaptive), _ptr(data), batched, C,
+            _i64_array(data.shape[2:]), int(padding), _ptr(sp), _ptr(grid_t), _ptr(out),
+            _stream(As.device)))
+    return out, grid_t, sp
+
+
+def warp_backward(ndim, nc, outsize, axes, As, n_stages, nstepsolver, adaptive, data, padding,
+                  stage_points, grid_t, grad_out, want_data, order=None):
+    """Returns (moments [n_stages * n_theta, nC, ppc], grad_data shaped like
+    data, or None)."""
+    _require(data, "data")
+    _require(As, "As")
+    _require(grid_t, "grid_t")
+    _require(grad_out, "grad")
+    n_theta, nC, C = As.shape[0] // n_stages, As.shape[1], data.shape[1]
+    moments = torch.empty((n_stages * n_theta, nC, ndim * (ndim + 1)), device=As.device,
+                          dtype=torch.float32)
+    gd = torch.empty_like(data) if want_data else None
+    batched = _data_batched(data, n_theta)
+    with _on(As.device):
+        _check(lib().cpab_b200_warp_backward(
+            ndim, _i32_array(nc), _i64_array(outsize), _ptr(axes), _ptr(order), _ptr(As),
+            n_stages, n_theta, int(nstepsolver), int(adaptive), _ptr(data), batched, C,
+            _i64_array(data.shape[2:]), int(padding), _ptr(stage_points), _ptr(grid_t),
+            _ptr(grad_out), _ptr(moments), _ptr(gd), _stream(As.device)))
     return moments, gd
 
 

@@ -149,18 +149,10 @@ def transform(points, theta, params, compute_points_grad=False, group=None):
     if group is not None and theta.requires_grad:
         theta = theta.view_as(theta)
         theta.register_hook(_allreduce_grad(group))
-    try:
-        return ext.transform(points_c, theta, basis.tensors, basis.d, basis.dense, _nc(params),
-                             int(params.nstepsolver),
-                             bool(getattr(params, "adaptive_substeps", False)),
-                             _order(params, points_c, batched), compute_points_grad, batched)
-    except RuntimeError as e:
-        # a failed C ABI call (the node's message starts with the library's
-        # name) raises the same error type as the Python path
-        first = str(e).split("\n", 1)[0]
-        if first.startswith("libcpab_b200: "):
-            raise _native.CpabNativeError(first[len("libcpab_b200: "):]) from None
-        raise
+    return _ext.call(ext.transform, points_c, theta, basis.tensors, basis.d, basis.dense,
+                     _nc(params), int(params.nstepsolver),
+                     bool(getattr(params, "adaptive_substeps", False)),
+                     _order(params, points_c, batched), compute_points_grad, batched)
 
 
 def _layout(points, theta, params):

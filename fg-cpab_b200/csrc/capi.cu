@@ -454,6 +454,90 @@ int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t
   return cuda_status(cpab::launch_transform_data_backward(a, m, stream), "transform_data_backward");
 }
 
+namespace {
+
+// Arguments shared by cpab_b200_warp and cpab_b200_warp_backward, on top of
+// check_mesh's: the chain length, the stage buffer, the padding mode and
+// whether every transformation has its own image.
+int check_warp(const char *fn, int n_stages, const float *stage_points, int data_batched,
+               int padding_mode, cpab::IntegrateArgs &a, cpab::MeshArgs &m) {
+  if (n_stages < 1 || n_stages > 4096)
+    return fail(CPAB_ERR_ARG, "%s: n_stages must be in [1, 4096], got %d", fn, n_stages);
+  if (data_batched != 0 && data_batched != 1)
+    return fail(CPAB_ERR_ARG, "%s: data_batched must be 0 or 1", fn);
+  if (padding_mode != cpab::kPadZeros && padding_mode != cpab::kPadBorder &&
+      padding_mode != cpab::kPadReflection)
+    return fail(CPAB_ERR_ARG, "%s: padding_mode must be 0 (zeros), 1 (border) or 2 (reflection)",
+                fn);
+  if (n_stages > 1 && a.nP > 0 && a.n_theta > 0 && stage_points == nullptr)
+    return fail(CPAB_ERR_ARG, "%s: null stage_points with %d stages", fn, n_stages);
+  const int64_t plane = (int64_t)m.in_size[0] * m.in_size[1] * m.in_size[2];
+  a.n_stages = n_stages;
+  a.stage_points = const_cast<float *>(stage_points);
+  m.data_bstride = data_batched ? (int64_t)m.C * plane : 0;
+  m.padding = padding_mode;
+  return CPAB_OK;
+}
+
+}  // namespace
+
+int cpab_b200_warp(int ndim, const int32_t *nc, const int64_t *out_size, const float *mesh_axes,
+                   const int32_t *order, const float *trels, const float *As, int n_stages,
+                   int n_theta, int nstepsolver, int adaptive, const float *data,
+                   int data_batched, int n_channels, const int64_t *in_size, int padding_mode,
+                   float *stage_points, float *grid_t, float *out, cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  cpab::MeshArgs m;
+  int st = check_mesh("warp", ndim, nc, out_size, mesh_axes, order, As, n_theta, nstepsolver,
+                      adaptive, data, n_channels, in_size, grid_t, a, m);
+  if (st != CPAB_OK) return st;
+  st = check_warp("warp", n_stages, stage_points, data_batched, padding_mode, a, m);
+  if (st != CPAB_OK) return st;
+  if (n_theta == 0 || a.nP == 0) return ok();
+  if (trels == nullptr || !aligned16(trels))
+    return fail(CPAB_ERR_ARG, "warp: trels must be non-null and 16-byte aligned");
+  if (out == nullptr && n_channels > 0) return fail(CPAB_ERR_ARG, "warp: null output");
+  a.trels = trels;
+  m.out = out;
+  return cuda_status(cpab::launch_warp(a, m, stream), "warp");
+}
+
+int cpab_b200_warp_backward(int ndim, const int32_t *nc, const int64_t *out_size,
+                            const float *mesh_axes, const int32_t *order, const float *As,
+                            int n_stages, int n_theta, int nstepsolver, int adaptive,
+                            const float *data, int data_batched, int n_channels,
+                            const int64_t *in_size, int padding_mode, const float *stage_points,
+                            const float *grid_t, const float *grad_out, float *moments,
+                            float *grad_data, cpab_stream_t stream) {
+  cpab::IntegrateArgs a;
+  cpab::MeshArgs m;
+  int st = check_mesh("warp_backward", ndim, nc, out_size, mesh_axes, order, As, n_theta,
+                      nstepsolver, adaptive, data, n_channels, in_size, grid_t, a, m);
+  if (st != CPAB_OK) return st;
+  st = check_warp("warp_backward", n_stages, stage_points, data_batched, padding_mode, a, m);
+  if (st != CPAB_OK) return st;
+  if (n_theta == 0) return ok();
+  if (moments == nullptr || !aligned16(moments))
+    return fail(CPAB_ERR_ARG, "warp_backward: moments must be non-null and 16-byte aligned");
+  if (grad_out == nullptr && a.nP > 0 && n_channels > 0)
+    return fail(CPAB_ERR_ARG, "warp_backward: null grad_out");
+  const size_t mbytes = (size_t)n_stages * n_theta * a.nC * ndim * (ndim + 1) * sizeof(float);
+  cudaError_t e = cudaMemsetAsync(moments, 0, mbytes, stream);
+  if (e != cudaSuccess) return cuda_status(e, "warp_backward: clearing moments");
+  if (grad_data != nullptr) {
+    const int64_t images = data_batched ? n_theta : 1;
+    const int64_t plane = (int64_t)m.in_size[0] * m.in_size[1] * m.in_size[2];
+    e = cudaMemsetAsync(grad_data, 0, (size_t)(images * n_channels * plane) * sizeof(float),
+                        stream);
+    if (e != cudaSuccess) return cuda_status(e, "warp_backward: clearing grad_data");
+  }
+  if (a.nP == 0 || n_channels == 0) return ok();  // zero upstream gradient
+  m.grad_out = grad_out;
+  m.grad_data = grad_data;
+  a.moments = moments;
+  return cuda_status(cpab::launch_warp_backward(a, m, stream), "warp_backward");
+}
+
 int cpab_b200_interpolate(int ndim, const float *data, int n_batch, int n_channels,
                           const int64_t *in_size, const float *grid, const int64_t *out_size,
                           float *out, cpab_stream_t stream) {

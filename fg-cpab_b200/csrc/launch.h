@@ -49,12 +49,24 @@ struct MeshArgs {
   float *out;              // forward: [n_theta, C, P]
   const float *grad_out;   // backward: [n_theta, C, P]
   float *grad_data;        // backward, may be null (zeroed by the caller)
+  // Spatial-transformer warp (warp.cu) only: elements between the images of
+  // consecutive transformations in data / grad_data (0: one image shared by
+  // all), and F.grid_sample's padding mode (kPadZeros, kPadBorder,
+  // kPadReflection).
+  int64_t data_bstride;
+  int padding;
 };
+
+enum : int { kPadZeros = 0, kPadBorder = 1, kPadReflection = 2 };
 
 // Each returns cudaSuccess or the launch error.
 cudaError_t launch_transform_data(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s);
 cudaError_t launch_transform_data_backward(const IntegrateArgs &a, const MeshArgs &m,
                                            cudaStream_t s);
+// Spatial-transformer warp: chains of a.n_stages stages over the meshgrid,
+// sampled as F.grid_sample(align_corners=True) samples (warp.cu).
+cudaError_t launch_warp(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s);
+cudaError_t launch_warp_backward(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s);
 cudaError_t launch_forward(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_forward_1d(const IntegrateArgs &a, cudaStream_t s);
 cudaError_t launch_backward(const IntegrateArgs &a, cudaStream_t s);

@@ -154,6 +154,143 @@ class TransformFunction : public torch::autograd::Function<TransformFunction> {
   }
 };
 
+// As (and Trels) of n rows of theta [n, d] through the basis B (transposed
+// operands for dense bases, as the Python build_A helper).
+std::pair<Tensor, Tensor> build_tables(const Basis &B, int nd, int64_t nC, const Tensor &th,
+                                       int64_t T, cpab_stream_t s) {
+  const int64_t n = th.size(0);
+  Tensor As = at::empty({n, nC, nd, nd + 1}, th.options());
+  Tensor trels = at::empty_like(As);
+  const float dT = 1.0f / (float)T;
+  if (B.dense) {
+    Tensor th_t = th.t().contiguous();
+    check(cpab_b200_build_A_tt(nd, nC, B.d, (int)n, iptr(B.rowptr), iptr(B.colidx),
+                               fptr(B.vals), fptr(th_t), dT, fptr_mut(As), fptr_mut(trels), s));
+  } else {
+    check(cpab_b200_build_A(nd, nC, B.d, (int)n, iptr(B.rowptr), iptr(B.colidx), fptr(B.vals),
+                            fptr(th), dT, fptr_mut(As), fptr_mut(trels), s));
+  }
+  return {As, trels};
+}
+
+// dtheta [n, d] = B^T vec(moments[n]).
+Tensor project_moments(const Basis &B, const Tensor &moments, cpab_stream_t s) {
+  const int64_t n = moments.size(0);
+  const int64_t D = moments.numel() / n;
+  Tensor g = at::empty({n, B.d}, moments.options());
+  if (B.dense) {
+    Tensor mt = moments.reshape({n, D}).t().contiguous();
+    check(cpab_b200_project_tt(B.d, D, (int)n, iptr(B.t_rowptr), iptr(B.t_colidx),
+                               fptr(B.t_vals), fptr(mt), fptr_mut(g), s));
+  } else {
+    check(cpab_b200_project(B.d, D, (int)n, iptr(B.t_rowptr), iptr(B.t_colidx), fptr(B.t_vals),
+                            fptr(moments), fptr_mut(g), s));
+  }
+  return g;
+}
+
+// The fused spatial-transformer warp (cpab/pytorch/warp.py, _Warp): data
+// [B or 1, C, *size], thetas K tensors [B, d] (theta_K acts first: the chain
+// runs them reversed), pixel axes and their cell order.  Arguments after
+// thetas are constants; backward returns one gradient per forward input
+// (data, each theta, then the constants).
+class WarpFunction : public torch::autograd::Function<WarpFunction> {
+ public:
+  static constexpr int kConstArgs = 9;  // basis .. padding
+
+  static Tensor forward(AutogradContext *ctx, Tensor data, at::TensorList thetas,
+                        std::vector<Tensor> basis, int64_t d, bool dense,
+                        std::vector<int64_t> nc, int64_t nstepsolver, bool adaptive, Tensor axes,
+                        c10::optional<Tensor> order, int64_t padding) {
+    TORCH_CHECK(!thetas.empty(), "at least one theta is needed");
+    TORCH_CHECK(data.is_cuda() && data.scalar_type() == at::kFloat, "x must be a float32 CUDA tensor");
+    const c10::cuda::CUDAGuard guard(data.device());
+    const Basis B = basis_of(basis, d, dense);
+    const int nd = (int)nc.size();
+    const int64_t nC = cells(nc), K = (int64_t)thetas.size(), n = thetas[0].size(0);
+    std::vector<Tensor> stages(thetas.rbegin(), thetas.rend());  // stage 0 = theta_K
+    for (const Tensor &t : stages)
+      TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.dim() == 2 &&
+                      t.size(0) == n && t.size(1) == d,
+                  "each theta must be a float32 CUDA tensor [B, ", d, "]");
+    const cpab_stream_t s = stream_of(data);
+    Tensor th = K == 1 ? stages[0].contiguous() : at::cat(stages, 0);
+    auto tabs = build_tables(B, nd, nC, th, nstepsolver, s);
+    Tensor data_c = data.contiguous();
+    std::vector<int64_t> size(data_c.sizes().begin() + 2, data_c.sizes().end());
+    int64_t P = 1;
+    for (int64_t v : size) P *= v;
+    std::vector<int64_t> out_shape{n, data_c.size(1)};
+    out_shape.insert(out_shape.end(), size.begin(), size.end());
+    Tensor out = at::empty(out_shape, data_c.options());
+    Tensor grid_t = at::empty({n, nd, P}, data_c.options());
+    Tensor sp = K > 1 ? at::empty({K - 1, n, nd, P}, data_c.options()) : Tensor();
+    Tensor ord = order.has_value() ? order->contiguous() : Tensor();
+    std::vector<int32_t> nc32(nc.begin(), nc.end());
+    const int batched = data_c.size(0) == n ? 1 : 0;
+    check(cpab_b200_warp(nd, nc32.data(), size.data(), fptr(axes), iptr(ord), fptr(tabs.second),
+                         fptr(tabs.first), (int)K, (int)n, (int)nstepsolver, adaptive ? 1 : 0,
+                         fptr(data_c), batched, (int)data_c.size(1), size.data(), (int)padding,
+                         fptr_mut(sp), fptr_mut(grid_t), fptr_mut(out), s));
+    ctx->save_for_backward({data_c, tabs.first, grid_t, axes});
+    ctx->saved_data["sp"] = sp;
+    ctx->saved_data["order"] = ord;
+    ctx->saved_data["basis"] = basis;
+    ctx->saved_data["d"] = d;
+    ctx->saved_data["dense"] = dense;
+    ctx->saved_data["nc"] = nc;
+    ctx->saved_data["T"] = nstepsolver;
+    ctx->saved_data["adaptive"] = adaptive;
+    ctx->saved_data["padding"] = padding;
+    ctx->saved_data["K"] = K;
+    return out;
+  }
+
+  static variable_list backward(AutogradContext *ctx, variable_list grads) {
+    auto saved = ctx->get_saved_variables();
+    Tensor data = saved[0], As = saved[1], grid_t = saved[2], axes = saved[3];
+    const c10::cuda::CUDAGuard guard(As.device());
+    const int64_t K = ctx->saved_data["K"].toInt();
+    bool want_theta = false;
+    for (int64_t i = 1; i <= K; ++i) want_theta = want_theta || ctx->needs_input_grad(i);
+    const bool want_data = ctx->needs_input_grad(0);
+    variable_list res(1 + K + kConstArgs);
+    if (!(want_data || want_theta)) return res;
+    const Basis B = basis_of(ctx->saved_data["basis"].toTensorVector(),
+                             ctx->saved_data["d"].toInt(), ctx->saved_data["dense"].toBool());
+    const std::vector<int64_t> nc = ctx->saved_data["nc"].toIntVector();
+    const int nd = (int)nc.size();
+    const int64_t nC = cells(nc), n = As.size(0) / K;
+    Tensor sp = ctx->saved_data["sp"].toTensor();
+    Tensor ord = ctx->saved_data["order"].toTensor();
+    std::vector<int64_t> size(data.sizes().begin() + 2, data.sizes().end());
+    std::vector<int32_t> nc32(nc.begin(), nc.end());
+    Tensor grad = grads[0].contiguous();
+    Tensor moments = at::empty({K * n, nC, nd * (nd + 1)}, As.options());
+    Tensor gd = want_data ? at::empty_like(data) : Tensor();
+    const cpab_stream_t s = stream_of(As);
+    check(cpab_b200_warp_backward(
+        nd, nc32.data(), size.data(), fptr(axes), iptr(ord), fptr(As), (int)K, (int)n,
+        (int)ctx->saved_data["T"].toInt(), ctx->saved_data["adaptive"].toBool() ? 1 : 0,
+        fptr(data), data.size(0) == n ? 1 : 0, (int)data.size(1), size.data(),
+        (int)ctx->saved_data["padding"].toInt(), fptr(sp), fptr(grid_t), fptr(grad),
+        fptr_mut(moments), fptr_mut(gd), s));
+    res[0] = gd;
+    if (want_theta) {
+      Tensor g = project_moments(B, moments, s);  // [K * n, d], stage-major
+      for (int64_t i = 0; i < K; ++i) res[1 + i] = g.narrow(0, (K - 1 - i) * n, n);
+    }
+    return res;
+  }
+};
+
+Tensor warp(Tensor data, std::vector<Tensor> thetas, std::vector<Tensor> basis, int64_t d,
+            bool dense, std::vector<int64_t> nc, int64_t nstepsolver, bool adaptive, Tensor axes,
+            c10::optional<Tensor> order, int64_t padding) {
+  return WarpFunction::apply(data, at::TensorList(thetas), basis, d, dense, nc, nstepsolver,
+                             adaptive, axes, order, padding);
+}
+
 Tensor transform(Tensor points, Tensor theta, std::vector<Tensor> basis, int64_t d, bool dense,
                  std::vector<int64_t> nc, int64_t nstepsolver, bool adaptive,
                  c10::optional<Tensor> order, bool compute_points_grad, bool batched) {
@@ -168,4 +305,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("transform", &transform,
         "points, theta, basis (6 CSR tensors of B and B^T), d, dense, nc, nstepsolver, "
         "adaptive, order or None, compute_points_grad, batched -> transformed points");
+  m.def("warp", &warp,
+        "x, thetas (list), basis (6 CSR tensors), d, dense, nc, nstepsolver, adaptive, pixel "
+        "axes, order or None, padding mode -> grid_sample of x on the warped pixel grid");
 }

@@ -307,6 +307,52 @@ int cpab_b200_transform_data_backward(int ndim, const int32_t *nc, const int64_t
                                       const float *grad_out, float *moments,
                                       float *grad_data, cpab_stream_t stream);
 
+/*
+ * Fused spatial-transformer warp (2D/3D): the CpabWarp layer of the
+ * reference's stn/stn.py:58-86,
+ *   out = F.grid_sample(data, T_1 o ... o T_K(pixel grid),
+ *                       align_corners=True, padding_mode),
+ * in one kernel.  K = n_stages transformations act on every output pixel,
+ * stage 0 first (the STN's T_K: its thetas reversed); As/trels are
+ * [n_stages, n_theta, nC, ppc] as for cpab_b200_forward_chain.  The pixel
+ * grid is the meshgrid of out_size whose axis values are mesh_axes, in CPAB
+ * coordinates: (linspace(-1, 1, n) + 1) / 2 per axis (0.5 for a one-pixel
+ * axis), the points stn/stn.py:43-46,80-82 build; CPAB coordinate k runs
+ * along image axis k.  data is [n_theta, n_channels, *in_size]
+ * (data_batched = 1) or one [n_channels, *in_size] image for all
+ * transformations (data_batched = 0); out is [n_theta, n_channels,
+ * *out_size].  padding_mode: 0 zeros, 1 border, 2 reflection (F.grid_sample's
+ * modes).  order (may be NULL): processing order of the output pixels, as
+ * for cpab_b200_transform_data.  stage_points ([n_stages-1, n_theta, ndim,
+ * P], may be NULL when n_stages == 1) and grid_t ([n_theta, ndim, P], the
+ * sampled positions) are written for the backward, both indexed by slot.
+ * The reference has no single native counterpart: it calls
+ * cpab/pytorch/transformer.py:28 once per transformation, then grid_sample.
+ */
+int cpab_b200_warp(int ndim, const int32_t *nc, const int64_t *out_size,
+                   const float *mesh_axes, const int32_t *order, const float *trels,
+                   const float *As, int n_stages, int n_theta, int nstepsolver,
+                   int adaptive, const float *data, int data_batched, int n_channels,
+                   const int64_t *in_size, int padding_mode, float *stage_points,
+                   float *grid_t, float *out, cpab_stream_t stream);
+
+/*
+ * Backward of cpab_b200_warp: grid_sample's gradient with respect to the
+ * sampled positions (and, when grad_data is non-NULL, the image), then the
+ * adjoint sweeps of all stages, last to first, in one kernel.  moments
+ * ([n_stages, n_theta, nC, ppc], 16-byte aligned) and grad_data (shaped like
+ * data) are zeroed here; the same order, stage_points and grid_t as the
+ * forward.
+ */
+int cpab_b200_warp_backward(int ndim, const int32_t *nc, const int64_t *out_size,
+                            const float *mesh_axes, const int32_t *order, const float *As,
+                            int n_stages, int n_theta, int nstepsolver, int adaptive,
+                            const float *data, int data_batched, int n_channels,
+                            const int64_t *in_size, int padding_mode,
+                            const float *stage_points, const float *grid_t,
+                            const float *grad_out, float *moments, float *grad_data,
+                            cpab_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -332,3 +332,148 @@ def interpolate_backward(ndim, data, grid, outsize, grad_out):
     for k in range(ndim):
         dgrid[:, k] = dgrid[:, k] * f(data.shape[2 + k] - 1)
     return dgrid, ddata.astype(f)
+
+
+# ---------------------------------------------------------------------------
+# The spatial-transformer sampling (stn/stn.py:48-54 of the reference):
+# F.grid_sample(x, grid, align_corners=True, padding_mode) bilinear (2D) /
+# trilinear (3D), at CPAB points p whose grid coordinate is g = 2p - 1
+# (stn/stn.py:86; CPAB coordinate k along image axis k).  Restates PyTorch
+# 2.11's rule (aten/src/ATen/native/GridSampler.h: unnormalisation and
+# padding; aten/src/ATen/native/cuda/GridSampler.cu: neighbours, weights and
+# gradients).  The source index is evaluated in float32 as there; weights
+# and sums in float64 (a checker, compared within tolerances).
+# ---------------------------------------------------------------------------
+
+GRID_SAMPLE_PADDING = {"zeros": 0, "border": 1, "reflection": 2}
+
+
+def _gs_index(p, n, padding):
+    """(source index [float32], d index / d g) along an axis of n pixels."""
+    f = np.float32
+    p = _f32(p)
+    g = (p * f(2) - f(1)).astype(f)
+    top = f(n - 1)
+    x = (((g + f(1)).astype(f) * f(0.5)).astype(f) * top).astype(f)
+    mult = np.full(x.shape, float(top) * 0.5)
+    if padding == "reflection":
+        if n == 1:
+            x = np.zeros_like(x)
+            mult = np.zeros_like(mult)
+        else:
+            sgn = np.where(x < 0, -1.0, 1.0)
+            a = np.abs(x)
+            extra = np.fmod(a, top).astype(f)
+            flips = np.floor((a / top).astype(f)).astype(np.int64)
+            odd = flips % 2 == 1
+            x = np.where(odd, (top - extra).astype(f), extra).astype(f)
+            mult = mult * np.where(odd, -sgn, sgn)
+    if padding in ("border", "reflection"):
+        clamped = (x <= 0) | (x >= top)
+        x = np.clip(x, f(0), top).astype(f)
+        mult = np.where(clamped, 0.0, mult)
+    bad = ~((x <= f(2.0 ** 31)) & (x >= f(-2.0 ** 31)))
+    x = np.where(bad, f(-100.0), x).astype(f)
+    return x, mult
+
+
+def _gs_taps(in_size, pts, padding):
+    """Per point: per axis (lo, fl, fh, mult) and the corner list."""
+    nd = len(in_size)
+    axes = []
+    for k in range(nd):
+        x, mult = _gs_index(pts[k], in_size[k], padding)
+        lo = np.floor(x).astype(np.int64)
+        xd = x.astype(np.float64)
+        axes.append((lo, (lo + 1) - xd, xd - lo, mult))
+    corners = []
+    for m in range(1 << nd):
+        hi = [(m >> (nd - 1 - k)) & 1 for k in range(nd)]
+        idx = [axes[k][0] + hi[k] for k in range(nd)]
+        inside = np.ones(pts.shape[1], dtype=bool)
+        for k in range(nd):
+            inside &= (idx[k] >= 0) & (idx[k] < in_size[k])
+        fac = [axes[k][2] if hi[k] else axes[k][1] for k in range(nd)]
+        corners.append((hi, [np.where(inside, i, 0) for i in idx], inside, fac))
+    return axes, corners
+
+
+def grid_sample_points(data, pts, padding="zeros"):
+    """data [B or 1, C, *in], pts [B, ndim, P] (CPAB coordinates) ->
+    [B, C, P]: the STN's F.grid_sample of data at the points."""
+    data = np.asarray(data, dtype=np.float64)
+    pts = _f32(pts)
+    B, nd, P = pts.shape
+    C = data.shape[1]
+    in_size = data.shape[2:]
+    out = np.zeros((B, C, P))
+    for b in range(B):
+        img = data[b if data.shape[0] > 1 else 0]
+        _, corners = _gs_taps(in_size, pts[b], padding)
+        for hi, idx, inside, fac in corners:
+            w = np.prod(fac, axis=0)
+            v = img[(slice(None),) + tuple(idx)]                  # [C, P]
+            out[b] += np.where(inside, v * w, 0.0)
+    return out.astype(np.float32)
+
+
+def grid_sample_points_backward(data, pts, grad_out, padding="zeros"):
+    """Gradients of grid_sample_points: (d pts [B, ndim, P] -- the CPAB
+    coordinates, i.e. twice the grid gradient --, d data shaped like data)."""
+    data = np.asarray(data, dtype=np.float64)
+    pts = _f32(pts)
+    g = np.asarray(grad_out, dtype=np.float64)
+    B, nd, P = pts.shape
+    in_size = data.shape[2:]
+    dpts = np.zeros((B, nd, P))
+    ddata = np.zeros(data.shape)
+    for b in range(B):
+        bi = b if data.shape[0] > 1 else 0
+        img = data[bi]
+        axes, corners = _gs_taps(in_size, pts[b], padding)
+        gk = np.zeros((nd, P))
+        for hi, idx, inside, fac in corners:
+            v = img[(slice(None),) + tuple(idx)]                  # [C, P]
+            vg = np.where(inside, (v * g[b]).sum(axis=0), 0.0)   # sum over channels
+            w = np.prod(fac, axis=0)
+            for k in range(nd):
+                other = np.prod([fac[j] for j in range(nd) if j != k], axis=0) if nd > 1 else 1.0
+                gk[k] += (1.0 if hi[k] else -1.0) * vg * other
+            for c in range(data.shape[1]):
+                np.add.at(ddata[bi, c], tuple(i[inside] for i in idx), (w * g[b, c])[inside])
+        for k in range(nd):
+            dpts[b, k] = 2.0 * axes[k][3] * gk[k]
+    return dpts.astype(np.float32), ddata.astype(np.float32)
+
+
+def warp_forward(nc, basis, data, thetas, axes, padding="zeros", nstepsolver=50):
+    """The STN layer's forward (stn/stn.py:40-54,79-86) from the oracle's
+    pieces: thetas [theta_1, ..., theta_K] (each [B, d]), theta_K acting
+    first on the pixel grid whose CPAB coordinates per axis are `axes`
+    ((linspace(-1, 1, n) + 1) / 2 as torch evaluates it).  Returns
+    (out [B, C, *out_size], the sampled points, per stage (points in, As))."""
+    nd = len(nc)
+    axes = [_f32(a) for a in axes]
+    out_size = [len(a) for a in axes]
+    mesh = np.meshgrid(*axes, indexing="ij")
+    pts = np.stack([m.reshape(-1) for m in mesh]).astype(np.float32)
+    stages = []
+    for theta in reversed(list(thetas)):
+        As = build_A(basis, theta, nd)
+        trels = expm(As, 1.0 / nstepsolver)
+        stages.append((pts, As))
+        pts = integrate(nc, pts, As, trels, nstepsolver)
+    out = grid_sample_points(data, pts, padding)
+    return out.reshape(out.shape[0], out.shape[1], *out_size), pts, stages
+
+
+def warp_backward(nc, basis, data, final_pts, stages, grad_out, padding="zeros",
+                  nstepsolver=50):
+    """Gradients of warp_forward: (d thetas in the order of thetas, d data)."""
+    g = np.asarray(grad_out, dtype=np.float32).reshape(grad_out.shape[0], grad_out.shape[1], -1)
+    lam, ddata = grid_sample_points_backward(data, final_pts, g, padding)
+    grads = []
+    for pts, As in reversed(stages):  # last stage first
+        mom, lam = adjoint(nc, pts, As, lam, nstepsolver, False, True)
+        grads.append(project(basis, mom))
+    return grads, ddata

@@ -150,6 +150,41 @@ def test_chain_entry_points_validate():
     assert f(2, NC2, P, 0, 0, None, P, P, 3, 1, 50, 0, P, P, None) == 0  # no points
 
 
+def test_warp_entry_points_validate():
+    L = _native.lib()
+    f, g = L.cpab_b200_warp, L.cpab_b200_warp_backward
+    err = lambda: L.cpab_b200_last_error().decode()  # noqa: E731
+    sz = (ctypes.c_int64 * 2)(8, 8)
+    # ndim, nc, out_size, axes, order, trels, As, n_stages, n_theta, T, adaptive, data,
+    # data_batched, C, in_size, padding, stage_points, grid_t, out, stream
+    ok = [2, NC2, sz, P, None, P, P, 1, 1, 50, 0, P, 1, 1, sz, 0, None, P, P, None]
+
+    def call(fn, base, **kw):
+        a = list(base)
+        for i, v in kw.items():
+            a[int(i[1:])] = v
+        return fn(*a)
+
+    assert call(f, ok, a0=1) == -1 and "ndim" in err()
+    assert call(f, ok, a15=3) == -1 and "padding_mode" in err()
+    assert call(f, ok, a15=-1) == -1
+    assert call(f, ok, a12=2) == -1 and "data_batched" in err()
+    assert call(f, ok, a7=0) == -1 and "n_stages" in err()
+    assert call(f, ok, a7=5000) == -1
+    assert call(f, ok, a7=2) == -1 and "stage_points" in err()
+    assert call(f, ok, a5=None) == -1 and "trels" in err()
+    assert call(f, ok, a9=0) == -2
+    assert call(f, ok, a8=70000) == -4
+    assert call(f, ok, a18=None) == -1 and "output" in err()
+    assert call(f, ok, a8=0) == 0                        # no transformations: nothing to do
+    # backward: ..., padding, stage_points, grid_t, grad_out, moments, grad_data, stream
+    okb = [2, NC2, sz, P, None, P, 1, 1, 50, 0, P, 1, 1, sz, 0, None, P, P, P, None, None]
+    assert call(g, okb, a18=None) == -1 and "moments" in err()
+    assert call(g, okb, a14=7) == -1 and "padding_mode" in err()
+    assert call(g, okb, a6=2) == -1 and "stage_points" in err()
+    assert call(g, okb, a17=None) == -1 and "grad_out" in err()
+
+
 def test_errors_are_per_thread():
     import threading
     L = _native.lib()
