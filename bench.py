@@ -80,7 +80,7 @@ def profiled_str(key):
 
 
 ORDER_NOTE = "points sorted by cell inside every timed step (no order kept across steps)"
-MESH_ORDER_NOTE = ("meshgrid points generated in the kernels; 3D visits them in a cell order "
+MESH_ORDER_NOTE = ("meshgrid points generated in the kernels and visited in a cell order "
                    "that depends only on the tessellation and output size, computed once")
 
 
@@ -390,6 +390,40 @@ def make_workload(name, rank, world, dev, unfused=False):
             return loss, t.grad
         return w, C, host, step, B * int(np.prod(outsize))
 
+    if name in ("stn2d", "stn3d"):
+        from cpab.pytorch.warp import CpabWarp, warp_composed
+        if name == "stn2d":   # the layer of the reference's stn/demos/demo_2d.py
+            tess, pad, B, shape, scale = (3, 3), "border", 32, [3, 128, 128], 0.7
+        else:                 # and of stn/demos/demo_3d.py
+            tess, pad, B, shape, scale = (4, 4, 4), "zeros", 32, [1, 32, 32, 32], 1.0
+        K = 2
+        nd = len(tess)
+        layer = CpabWarp(tess, padding_mode=pad)
+        w = Workload(name, "%dD CpabWarp(%s, padding_mode=%r): %d images %s, the composition "
+                     "T_1 o T_2 of %d transformations theta~N(0,%g^2) (stn/stn.py:58-86), MSE to "
+                     "a second batch, backward to both thetas; each GPU its own batch"
+                     % (nd, tess, pad, B, shape, K, scale),
+                     list(tess), True, B, K, "weak", "batch-parallel over %d GPU(s), no collective"
+                     % world)
+        C = layer.cpab
+        w.warp_data = (shape[0], int(np.prod(shape[1:])))  # channels, image plane
+        g = gen(2 + 10 * rank)
+        host = {"theta": torch.randn(K, B, C.params.d, generator=gen(0)) * scale,
+                "data": torch.rand(B, *shape, generator=g),
+                "target": torch.rand(B, *shape, generator=g)}
+        if unfused:
+            del w.warp_data
+            w.desc += " (unfused: the reference layer's CPAB_transformer calls + F.grid_sample)"
+
+        def step(x):
+            t = x["theta"].requires_grad_(True)
+            out = (warp_composed(x["data"], list(t), C.params, pad) if unfused
+                   else layer(x["data"], t))
+            loss = F.mse_loss(out, x["target"])
+            loss.backward()
+            return loss, t.grad
+        return w, C, host, step, B * int(np.prod(shape[1:])) * K
+
     if name == "chain3d":
         tess, K, grid_n = [16, 16, 16], 4, [160, 192, 160]
         w = Workload(name, "3D Cpab([16,16,16], zero_boundary=True): transform_grid_chain, 4 stages, "
@@ -465,7 +499,7 @@ KERNELS_PER_CALL = {"build_A": 1, "build_A_tt": 1, "order_points": 3, "project":
                     "project_tt": 1, "interpolate": 1,
                     "interpolate_backward": 1, "expm": 1, "forward": 1, "backward": 1,
                     "transform_data": 1, "transform_data_backward": 1, "forward_chain": 1,
-                    "backward_chain": 1}
+                    "backward_chain": 1, "warp": 1, "warp_backward": 1}
 
 
 class PhaseTimer:
@@ -696,10 +730,14 @@ def run_ours(args, rank, world, local):
     default = args.config == "2d"
 
     fused = getattr(w, "fused_data", None) is not None
-    chain = w.stages > 1 and C.params.ndim in (2, 3)   # one launch through all stages
-    # the integration calls of this workload (for transform_data the fused
-    # resample-integration kernels)
+    warped = getattr(w, "warp_data", None) is not None
+    stn = args.config.startswith("stn")
+    # one launch through all stages (the unfused STN runs one call per stage)
+    chain = w.stages > 1 and C.params.ndim in (2, 3) and not stn
+    # the integration calls of this workload (for transform_data and the STN
+    # warp the fused resample-integration kernels)
     names = (("transform_data", "transform_data_backward") if fused else
+             ("warp", "warp_backward") if warped else
              ("forward_chain", "backward_chain") if chain else ("forward", "backward"))
     timer = PhaseTimer(_native)
 
@@ -802,6 +840,11 @@ def run_ours(args, rank, world, local):
             ch, plane = w.fused_data
             bwd_bytes = (w.batch * (nd + ch) * pts_per_launch + w.batch * ch * plane
                          + 2 * w.batch * p.nC * ppc) * 4
+        elif warped:  # sampled grid, stage inputs, output gradient, images, tables
+            ch, plane = w.warp_data
+            K = w.stages
+            bwd_bytes = (w.batch * (K * nd + ch) * pts_per_launch + w.batch * ch * plane
+                         + 2 * K * w.batch * p.nC * ppc) * 4
         elif chain:  # all stages: saved stage inputs instead of recomputed ones
             K = w.stages
             bwd_bytes = (nd * pts_per_launch + w.batch * nd * pts_per_launch
@@ -827,7 +870,7 @@ def run_ours(args, rank, world, local):
             "workload": w.desc, "tess": w.tess, "batch": w.batch, "stages": w.stages,
             "nstepsolver": NSTEP, "global_batch": pairs_step, "parallelism": w.parallelism,
             "l2": "flushed between timed steps (%d MiB write)" % (L2_FLUSH_BYTES >> 20),
-            "point_order": (MESH_ORDER_NOTE if fused else
+            "point_order": (MESH_ORDER_NOTE if fused or warped else
                             "fixed meshgrid: its sort order is computed once and kept"
                             if keep_order else ORDER_NOTE)}
         line = {
@@ -839,6 +882,8 @@ def run_ours(args, rank, world, local):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm",
                          "kernel": "k_backward_mesh (fused resample + adjoint)" if fused
+                         else "k_backward_warp (fused grid_sample + adjoint, all stages)"
+                         if warped
                          else "k_backward (fused adjoint, all chain stages)" if chain
                          else "k_backward (fused adjoint)",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
@@ -898,9 +943,12 @@ def main():
                     help="skip timing the reference's own GPU kernels at N=1")
     ap.add_argument("--unfused", action="store_true",
                     help="dense2d / 3d: time the unfused composition (meshgrid, transform_grid, "
-                         "interpolate) instead of the fused transform_data kernels")
+                         "interpolate) instead of the fused transform_data kernels; stn2d / "
+                         "stn3d: the reference layer's composition (a CPAB_transformer call per "
+                         "transformation, then F.grid_sample) instead of the fused warp")
     ap.add_argument("--config", default="2d",
-                    choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d"],
+                    choices=["2d", "2d12", "2d30", "1d", "dense2d", "3d", "chain3d", "stn2d",
+                             "stn3d"],
                     help="workload (default: BASELINE configs[1], 2D 20x20)")
     args = ap.parse_args()
     if args.impl == "reference":

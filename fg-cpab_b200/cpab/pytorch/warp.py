@@ -94,6 +94,27 @@ def warp(x, thetas, params, padding_mode="zeros"):
                      axes, order, PADDING_MODES[padding_mode])
 
 
+def warp_composed(x, thetas, params, padding_mode="zeros"):
+    """The reference layer's composition, step by step (stn/stn.py:40-54 with
+    CpabWarp.transform, :79-86): the pixel grid in [-1, 1], one
+    CPAB_transformer call per theta (the last first), then F.grid_sample;
+    1D samples a [B, C, 1, W] image at y = 0.  The 1D path of CpabWarp, and
+    the unfused baseline of warp() in 2D and 3D."""
+    size = x.shape[2:]
+    f32 = dict(device=x.device, dtype=torch.float32)
+    axes = [torch.linspace(-1, 1, n, **f32) if n > 1 else torch.zeros(1, **f32) for n in size]
+    points = torch.stack(torch.meshgrid(*axes, indexing="ij")[::-1]).flatten(1)  # (x, y, z)
+    points = (points.flip(-2) + 1) / 2          # CPAB coordinates on [0, 1]
+    for theta in reversed(list(thetas)):
+        points = CPAB_transformer(points, theta, params, points.requires_grad)
+    grid = (points * 2 - 1).flip(-2).transpose(1, 2).reshape(len(points), *size, -1)
+    if len(size) == 1:
+        out = F.grid_sample(x.unsqueeze(2), F.pad(grid, (0, 1)).unsqueeze(1),
+                            align_corners=True, padding_mode=padding_mode)
+        return out.squeeze(2)
+    return F.grid_sample(x, grid, align_corners=True, padding_mode=padding_mode)
+
+
 class _Warp(torch.autograd.Function):
     """The chain of K transformations runs stage 0 first, so the stages are
     thetas reversed (the STN's T_K acts first); A/Trels of all K*B rows come
@@ -170,20 +191,6 @@ class CpabWarp(nn.Module):
         thetas = [theta] if torch.is_tensor(theta) and theta.dim() == 2 else list(theta)
         with torch.autocast(x.device.type, enabled=False):
             thetas = [th.float() for th in thetas]
-            if self.ndim > 1:
-                out = warp(x.float(), thetas, self.cpab.params, self.padding_mode)
-            else:
-                out = self._sample_1d(x.float(), thetas)
+            fn = warp if self.ndim > 1 else warp_composed
+            out = fn(x.float(), thetas, self.cpab.params, self.padding_mode)
         return out.to(x.dtype)
-
-    def _sample_1d(self, x, thetas):
-        """1D: the pixel grid through CPAB_transformer, then grid_sample of the
-        [B, C, 1, W] image at y = 0 (the reference's composition)."""
-        f32 = dict(device=x.device, dtype=torch.float32)
-        n = x.shape[2]
-        pixels = torch.linspace(-1, 1, n, **f32) if n > 1 else torch.zeros(1, **f32)
-        grid = self.transform(pixels[None], thetas)                 # [B, 1, W]
-        grid = F.pad(grid.transpose(1, 2), (0, 1)).unsqueeze(1)     # [B, 1, W, 2] with y = 0
-        out = F.grid_sample(x.unsqueeze(2), grid, align_corners=True,
-                            padding_mode=self.padding_mode)
-        return out.squeeze(2)

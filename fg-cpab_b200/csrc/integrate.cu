@@ -354,9 +354,14 @@ template <int ND>
 cudaError_t forward_nd(const IntegrateArgs &a, cudaStream_t s) {
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
   if constexpr (ND > 1) {
-    if (a.n_stages > 1)  // fused chain: tables read through L1/L2
+    if (a.n_stages > 1) {  // fused chain: all stages' tables in shared memory when they fit
+      const size_t tabs = tab * (size_t)a.n_stages;
+      if (tabs <= kFwdSmemBudget)
+        return a.adaptive ? launch_wave(k_forward<ND, true, true, true>, kFwdThreads, tabs, a, s)
+                          : launch_wave(k_forward<ND, false, true, true>, kFwdThreads, tabs, a, s);
       return a.adaptive ? launch_wave(k_forward<ND, true, false, true>, kFwdThreads, 0, a, s)
                         : launch_wave(k_forward<ND, false, false, true>, kFwdThreads, 0, a, s);
+    }
   }
   const bool smem = tab <= kFwdSmemBudget;
   if (a.adaptive) {
@@ -378,10 +383,29 @@ cudaError_t backward_launch(const IntegrateArgs &a, size_t smem, size_t cl, cuda
   return launch_wave(k_backward<ND, ADAPT, A_SMEM, M_SMEM, false, CellT>, kT, smem, a, s);
 }
 
-// Fused chains: tables stay in global memory (stage after stage per thread).
+// Fused chains (stage after stage per thread): all stages' tables (tabs
+// bytes) in shared memory when they fit beside the cell record -- in 2D one
+// 1024-thread block per SM, as for single transformations -- else in global
+// memory.
 template <int ND, bool ADAPT, typename CellT>
-cudaError_t backward_chain_launch(const IntegrateArgs &a, size_t cl, cudaStream_t s) {
+cudaError_t backward_chain_launch(const IntegrateArgs &a, size_t tabs, size_t cl,
+                                  cudaStream_t s) {
   constexpr int kT = BwdShape<ND>::kThreads;
+  if constexpr (ND == 2 && !ADAPT && sizeof(CellT) == 2) {
+    constexpr int kW = BwdShape<ND, true>::kThreads;
+    const size_t cl_wide = (size_t)kW * a.T * sizeof(CellT);
+    if (tabs + cl_wide <= kBwdWideSmemBudget)
+      return launch_wave(k_backward<ND, false, true, false, true, CellT, true, true>, kW,
+                         tabs + cl_wide, a, s);
+  }
+  if (tabs <= kBwdSmemBudget) {
+    if constexpr (!ADAPT && sizeof(CellT) == 2) {
+      if (cl > 0 && tabs + cl <= kBwdSmemBudget)
+        return launch_wave(k_backward<ND, ADAPT, true, false, true, CellT, true>, kT, tabs + cl,
+                           a, s);
+    }
+    return launch_wave(k_backward<ND, ADAPT, true, false, false, CellT, true>, kT, tabs, a, s);
+  }
   if constexpr (!ADAPT && sizeof(CellT) == 2) {
     if (cl > 0)
       return launch_wave(k_backward<ND, ADAPT, false, false, true, CellT, true>, kT, cl, a, s);
@@ -409,7 +433,8 @@ cudaError_t backward_cells(const IntegrateArgs &a, cudaStream_t s) {
       return backward_launch<ND, ADAPT, true, true, CellT>(a, 2 * tab, cl_fits(2 * tab), s);
   }
   if constexpr (ND > 1) {
-    if (a.n_stages > 1) return backward_chain_launch<ND, ADAPT, CellT>(a, cl_fits(0), s);
+    if (a.n_stages > 1)
+      return backward_chain_launch<ND, ADAPT, CellT>(a, tab * (size_t)a.n_stages, cl_fits(0), s);
   }
   if (tab <= kBwdSmemBudget)
     return backward_launch<ND, ADAPT, true, false, CellT>(a, tab, cl_fits(tab), s);

@@ -86,16 +86,23 @@ __device__ __forceinline__ void mesh_point(const MeshArgs &m, int64_t o, float (
 // cpab/core/cpab_ops_2d.cu:212-278, cpab/core/cpab_ops_3d.cu:169-241.
 // ---------------------------------------------------------------------------
 
-// CHAIN: a.n_stages transformations per point (fused chains; tables are
-// never staged then).  Without it the stage loop compiles away.
+// CHAIN: a.n_stages transformations per point (fused chains; with SMEM all
+// stages' tables are staged, one after another).  Without it the stage loop
+// compiles away.
 template <int ND, bool ADAPT, bool SMEM, bool CHAIN, class Src>
 __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &src) {
   constexpr int P = Dim<ND>::kPpc;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
   const int b = blockIdx.y;
-  if constexpr (SMEM) {
-    stage_table<ND>(s_tab, a.trels + (int64_t)b * a.nC * P, a.nC);
+  if constexpr (SMEM) {  // a fused chain stages every stage's table, one after another
+    if constexpr (CHAIN) {
+      for (int st = 0; st < a.n_stages; ++st)
+        stage_table<ND>(s_tab + (size_t)st * a.nC * P,
+                        a.trels + ((int64_t)st * a.n_theta + b) * a.nC * P, a.nC);
+    } else {
+      stage_table<ND>(s_tab, a.trels + (int64_t)b * a.nC * P, a.nC);
+    }
     __syncthreads();
   }
   const Tess t = a.tess;
@@ -110,7 +117,7 @@ __device__ __forceinline__ void forward_body(const IntegrateArgs &a, const Src &
     src.start(slot, i, p);
     for (int st = 0; st < nst; ++st) {
     const int64_t off = ((int64_t)st * a.n_theta + b) * a.nC * P;
-    const float *tab = SMEM ? s_tab : a.trels + off;
+    const float *tab = SMEM ? (CHAIN ? s_tab + (size_t)st * a.nC * P : s_tab) : a.trels + off;
     const float *ag = a.As + off;
     // Unrolled by a divisor of the usual T = 50 (loop control is ~4% of a step);
     // measured: 2D 139 -> 136 us, 3D 971 -> 940 us on the bench shapes.
@@ -174,13 +181,22 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
   constexpr int S = kSegSteps;
   extern __shared__ float4 smem4[];
   float *s_tab = reinterpret_cast<float *>(smem4);
-  float *s_mom = s_tab + (A_SMEM ? a.nC * P : 0);
+  // With A_SMEM the table (a fused chain: every stage's table) comes first.
+  float *s_mom = s_tab + (A_SMEM ? (CHAIN ? a.n_stages * a.nC * P : a.nC * P) : 0);
   CellT *s_cl = reinterpret_cast<CellT *>(s_mom + (M_SMEM ? a.nC * P : 0)) + threadIdx.x;
   const int b = blockIdx.y;
   const int nC = a.nC;
   const float *ag = a.As + (int64_t)b * nC * P;
   float *gm = a.moments + (int64_t)b * nC * P;
-  if constexpr (A_SMEM) stage_table<ND>(s_tab, ag, nC);
+  if constexpr (A_SMEM) {
+    if constexpr (CHAIN) {
+      for (int st = 0; st < a.n_stages; ++st)
+        stage_table<ND>(s_tab + (size_t)st * nC * P,
+                        a.As + ((int64_t)st * a.n_theta + b) * nC * P, nC);
+    } else {
+      stage_table<ND>(s_tab, ag, nC);
+    }
+  }
   if constexpr (M_SMEM) {
     for (int i = threadIdx.x; i < nC * P; i += blockDim.x) s_mom[i] = 0.0f;
   }
@@ -209,7 +225,7 @@ __device__ __forceinline__ void backward_body(const IntegrateArgs &a, const Src 
     const int nst = CHAIN ? a.n_stages : 1;
     for (int st = nst - 1; st >= 0; --st) {
     if constexpr (CHAIN) {
-      tab = a.As + ((int64_t)st * a.n_theta + b) * nC * P;
+      tab = A_SMEM ? s_tab + (size_t)st * nC * P : a.As + ((int64_t)st * a.n_theta + b) * nC * P;
       gm = a.moments + ((int64_t)st * a.n_theta + b) * nC * P;
     }
     float p[ND];

@@ -280,13 +280,18 @@ cudaError_t launch_warp_kernel(K kernel, int threads, size_t smem, const Integra
   return cudaGetLastError();
 }
 
-// Shared-memory choices as for the fused transform_data kernels; chains read
-// their per-stage tables through L1/L2.
+// Shared-memory choices as for the fused transform_data kernels; chains hold
+// all their stages' tables in shared memory when they fit (the STN's small
+// tessellations), else read them through L1/L2.
 template <int ND, bool ADAPT>
 cudaError_t warp_forward_nd(const IntegrateArgs &a, const MeshArgs &m, cudaStream_t s) {
-  if (a.n_stages > 1)
-    return launch_warp_kernel(k_forward_warp<ND, ADAPT, false, true>, kFwdThreads, 0, a, m, s);
   const size_t tab = (size_t)a.nC * Dim<ND>::kPpc * sizeof(float);
+  if (a.n_stages > 1) {
+    const size_t tabs = tab * (size_t)a.n_stages;
+    if (tabs <= kFwdSmemBudget)
+      return launch_warp_kernel(k_forward_warp<ND, ADAPT, true, true>, kFwdThreads, tabs, a, m, s);
+    return launch_warp_kernel(k_forward_warp<ND, ADAPT, false, true>, kFwdThreads, 0, a, m, s);
+  }
   if (tab <= kFwdSmemBudget)
     return launch_warp_kernel(k_forward_warp<ND, ADAPT, true, false>, kFwdThreads, tab, a, m, s);
   return launch_warp_kernel(k_forward_warp<ND, ADAPT, false, false>, kFwdThreads, 0, a, m, s);
@@ -299,6 +304,23 @@ cudaError_t warp_backward_cells(const IntegrateArgs &a, const MeshArgs &m, cudaS
   constexpr bool kCl = !ADAPT && sizeof(CellT) == 2;
   const size_t cl = kCl ? cell_record_bytes<ND, CellT>(kT, a.T) : 0;
   if (a.n_stages > 1) {
+    const size_t tabs = tab * (size_t)a.n_stages;
+    if constexpr (ND == 2 && kCl) {
+      constexpr int kW = BwdShape<ND, true>::kThreads;
+      const size_t cl_wide = (size_t)kW * a.T * sizeof(CellT);
+      if (tabs + cl_wide <= kBwdWideSmemBudget)
+        return launch_warp_kernel(k_backward_warp<ND, ADAPT, true, true, CellT, GD, true, true>,
+                                  kW, tabs + cl_wide, a, m, s);
+    }
+    if (tabs <= kBwdSmemBudget) {
+      if constexpr (kCl) {
+        if (tabs + cl <= kBwdSmemBudget)
+          return launch_warp_kernel(k_backward_warp<ND, ADAPT, true, true, CellT, GD, true>, kT,
+                                    tabs + cl, a, m, s);
+      }
+      return launch_warp_kernel(k_backward_warp<ND, ADAPT, true, false, CellT, GD, true>, kT,
+                                tabs, a, m, s);
+    }
     if constexpr (kCl) {
       if (cl <= kBwdSmemBudget)
         return launch_warp_kernel(k_backward_warp<ND, ADAPT, false, true, CellT, GD, true>, kT,

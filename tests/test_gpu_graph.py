@@ -72,7 +72,7 @@ def test_graphed_transform_grid_step_matches_eager(tess, nP):
         torch.cuda.synchronize()
         e_out, e_loss, e_grad = _eager(step, theta, pts.clone())
         assert torch.equal(out, e_out), rep
-        assert abs(float(loss) - float(e_loss)) <= 1e-6 * abs(float(e_loss)), rep
+        assert abs(float(loss.detach()) - float(e_loss)) <= 1e-6 * abs(float(e_loss)), rep
         assert _rel(grad, e_grad) < DTHETA_RTOL, rep
 
 

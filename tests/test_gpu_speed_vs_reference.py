@@ -78,3 +78,37 @@ def test_faster_than_reference_kernels():
         with open(path, "w") as f:
             json.dump(report, f, indent=1)
     assert ours["total"] < ref["total"]
+
+
+@pytest.mark.parametrize("case", ["stn2d", "stn3d"])
+def test_warp_faster_than_reference_layer(case):
+    """The fused spatial-transformer warp against the reference's CpabWarp
+    composition (stn/stn.py:40-54,79-86: a CPAB_transformer call per
+    transformation on the reference's kernels, then F.grid_sample), fwd+bwd
+    of a weighted sum on the demo layers' shapes (stn/demos/demo_2d.py,
+    demo_3d.py): 32 images, two composed transformations."""
+    import test_gpu_warp as W
+    from cpab.pytorch.warp import CpabWarp
+    tess, pad, shape, scale = (((3, 3), "border", (3, 128, 128), 0.7) if case == "stn2d"
+                               else ((4, 4, 4), "zeros", (1, 32, 32, 32), 1.0))
+    layer = CpabWarp(tess, padding_mode=pad)
+    g = torch.Generator("cuda").manual_seed(0)
+    x = torch.rand(32, *shape, device="cuda", generator=g)
+    ths = [(scale * torch.randn(32, layer.theta_dim, device="cuda", generator=g)).requires_grad_(True)
+           for _ in range(2)]
+    w = torch.randn(32, *shape, device="cuda", generator=g)
+
+    def step(fn):
+        def run():
+            for t in ths:
+                t.grad = None
+            (fn() * w).sum().backward()
+        return run
+
+    ours = _time(step(lambda: layer(x, ths)))
+    composed_ours = _time(step(lambda: W.composed(layer, x, ths)))
+    ref = _time(step(lambda: W.composed(layer, x, ths, W._RefTransformer.apply)))
+    print(json.dumps({"workload": case, "unit": "ms", "fused_warp": ours,
+                      "composition_on_this_library": composed_ours,
+                      "composition_on_reference_kernels": ref, "speedup_vs_reference": ref / ours}))
+    assert ours < ref
