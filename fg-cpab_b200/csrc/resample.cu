@@ -40,7 +40,7 @@ constexpr int kRows = 8;
 // (a separate instantiation, so the common grid-only backward carries no
 // scatter code).
 template <int ND, int MODE>
-__global__ void __launch_bounds__(kTile *kRows) k_interp(ResampleArgs a) {
+__device__ __forceinline__ void interp_body(const ResampleArgs &a) {
   __shared__ float sg[ND][kTile][kTile + 1];  // [i_last local][i0 local]
   const int C = a.n_channels;
   const int in[3] = {(int)a.in_size[0], (int)a.in_size[1], (int)a.in_size[2]};
@@ -116,6 +116,26 @@ __global__ void __launch_bounds__(kTile *kRows) k_interp(ResampleArgs a) {
   }
 }
 
+template <int ND, int MODE>
+__global__ void __launch_bounds__(kTile *kRows) k_interp(ResampleArgs a) {
+  interp_body<ND, MODE>(a);
+}
+
+// 2D forward and grid-only backward, compiled for 8 and 6 resident blocks per
+// SM (32 and 40 registers): their gathers are latency-bound, and the extra
+// resident warps hide more of it than the few spilled values cost.  Measured
+// at the dense 2D shape (32 x 3 x 512^2, CUDA events): forward 141 -> 115 us,
+// backward 199 -> 145 us (at 6 and 4 blocks: 120 and 167 us).  3D, whose
+// per-point state is larger, spills heavily under such caps and ran slower
+// (forward 113 -> 123 us at 4 blocks); it keeps the compiler's choice.
+template <int MODE> struct Interp2dBlocks { static constexpr int v = MODE == 0 ? 8 : 6; };
+
+template <int MODE>
+__global__ void __launch_bounds__(kTile *kRows, Interp2dBlocks<MODE>::v)
+    k_interp_2d(ResampleArgs a) {
+  interp_body<2, MODE>(a);
+}
+
 cudaError_t launch(const ResampleArgs &a, cudaStream_t s, bool bwd) {
   if (a.n_batch == 0 || a.n_channels == 0) return cudaSuccess;
   const dim3 block(kTile, kRows);
@@ -131,8 +151,8 @@ cudaError_t launch(const ResampleArgs &a, cudaStream_t s, bool bwd) {
     if (n0 == 0 || nl == 0) return cudaSuccess;
     const dim3 grid((unsigned)((nl + kTile - 1) / kTile), (unsigned)((n0 + kTile - 1) / kTile),
                     (unsigned)a.n_batch);
-    if (!bwd) k_interp<2, 0><<<grid, block, 0, s>>>(a);
-    else if (a.grad_data == nullptr) k_interp<2, 1><<<grid, block, 0, s>>>(a);
+    if (!bwd) k_interp_2d<0><<<grid, block, 0, s>>>(a);
+    else if (a.grad_data == nullptr) k_interp_2d<1><<<grid, block, 0, s>>>(a);
     else k_interp<2, 2><<<grid, block, 0, s>>>(a);
   } else {
     const int64_t n1 = a.out_size[1], nl = a.out_size[2];
