@@ -570,7 +570,7 @@ def source_sha():
     not reported as this build's."""
     import hashlib
     h = hashlib.sha256()
-    for f in ("cpab_device.cuh", "integrate.cu", "launch.h"):
+    for f in ("cpab_device.cuh", "integrate_body.cuh", "integrate.cu", "launch.h"):
         with open(os.path.join(ROOT, "fg-cpab_b200", "csrc", f), "rb") as fh:
             h.update(fh.read())
     return h.hexdigest()[:16]
