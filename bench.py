@@ -645,6 +645,13 @@ def strong_scaling(C, steps, warmup, flush, rank, world, timer):
         ms = timed_steps(fn, steps, flush, world)
         out[name] = {"value": BATCH * N_POINTS / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
                      "phase_ms": breakdown(fn, steps, flush, world, timer)[0]}
+        gms = graph_steps(fn, steps, flush, world, timer)
+        if gms is not None:
+            out[name]["graph_replay"] = {
+                "value": BATCH * N_POINTS / (gms * 1e-3), "unit": UNIT, "ms_per_step": gms,
+                "note": "each rank's step (sort, forward, loss, backward, projection and, "
+                        "points sharded, the dtheta allreduce) captured once in a CUDA graph "
+                        "and replayed: no host issue time, no rank drift from it"}
     out["points_sharded"]["how"] = ("the 125,000 points split over the ranks, all 16 "
                                     "transformations on every rank, one dtheta allreduce")
     out["batch_sharded"]["how"] = ("all 125,000 points on every rank, %d of the 16 "
@@ -652,6 +659,42 @@ def strong_scaling(C, steps, warmup, flush, rank, world, timer):
                                    % (BATCH // world))
     out["problem"] = "fixed: 125,000 points x batch 16 (2,000,000 pairs) whatever the GPU count"
     return out
+
+
+def graph_steps(fn, steps, flush, world, timer):
+    """ms per replay of fn() captured in one CUDA graph on every rank (its NCCL
+    allreduce included), max over ranks; None on every rank when any rank
+    could not capture it (agreed on before any replay, so that no rank
+    replays a collective the others never launch)."""
+    g, ok = None, 1.0
+    timer.capture = True
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+    except Exception as e:  # noqa: BLE001 -- reported, and agreed on below
+        print("graph capture failed: %r" % (e,), file=sys.stderr)
+        g, ok = None, 0.0
+    finally:
+        timer.capture = False
+    torch.cuda.synchronize()
+    flag = torch.tensor([ok], device="cuda")
+    if world > 1:
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if flag.item() < 1.0:
+        return None
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    ms = timed_steps(g.replay, steps, flush, world)
+    del g  # before the process group goes: a graph holding NCCL calls must not outlive it
+    return ms
 
 
 REF_KERNELS = os.path.join(ROOT, "oracle", "_ref", "libcpab_ref.so")
