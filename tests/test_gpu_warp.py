@@ -269,3 +269,27 @@ def test_cpp_node_matches_python_node():
     for a, b in zip(gth, rth):
         assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
     assert (gx - rx).abs().max().item() <= 1e-6
+
+
+# one-pixel axes (grid_sample's size-1 rules: the pixel at 0.5, reflection's
+# degenerate fold), a batch of one, every padding mode
+EDGE = [((3, 3), size, pad) for size in [(1, 1), (1, 6), (5, 1)]
+        for pad in ("zeros", "border", "reflection")] + \
+       [((2, 2, 2), size, pad) for size in [(1, 1, 1), (3, 1, 4)]
+        for pad in ("zeros", "border", "reflection")]
+
+
+@pytest.mark.parametrize("case", EDGE, ids=["%s-%s-%s" % ("x".join(map(str, t)), "x".join(map(str, s)), p)
+                                            for t, s, p in EDGE])
+def test_degenerate_images_match_the_composition(case):
+    tess, size, padding = case
+    layer = CpabWarp(tess, zero_boundary=False, padding_mode=padding)
+    x, thetas = _inputs(layer, 1, 2, size, 2, 17, 0.8)
+    w = torch.randn(1, 2, *size, device=DEV, generator=torch.Generator(DEV).manual_seed(4))
+    out, gth, gx = _run(lambda a, t: layer(a, t), x, thetas, w)
+    ref, rth, rx = _run(lambda a, t: composed(layer, a, t), x, thetas, w)
+    assert (out - ref).abs().max().item() <= OUT_ATOL
+    for a, b in zip(gth, rth):
+        na = float(b.norm())
+        assert float((a - b).norm()) <= DTHETA_RTOL * max(na, 1e-6)
+    assert (gx - rx).abs().max().item() <= OUT_ATOL
