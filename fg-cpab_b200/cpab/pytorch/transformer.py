@@ -161,6 +161,8 @@ def _layout(points, theta, params):
     n_theta = theta.shape[0]
     if theta.dim() != 2 or theta.shape[1] != params.d:
         raise ValueError("theta must be [n_batch, %d], got %s" % (params.d, tuple(theta.shape)))
+    if points.device != theta.device:
+        raise ValueError("points on %s, theta on %s" % (points.device, theta.device))
     if points.dim() == 2:
         if points.shape[0] != nd:
             raise ValueError("points must be [%d, n_points], got %s" % (nd, tuple(points.shape)))

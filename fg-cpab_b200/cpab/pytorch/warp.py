@@ -80,6 +80,8 @@ def warp(x, thetas, params, padding_mode="zeros"):
     for th in thetas:
         if th.dim() != 2 or th.shape[0] != B or th.shape[1] != params.d:
             raise ValueError("each theta must be [B, %d] with the same B" % params.d)
+        if th.device != x.device:
+            raise ValueError("theta on %s, x on %s" % (th.device, x.device))
     if x.shape[0] != B:
         raise ValueError("x holds %d images for %d transformations" % (x.shape[0], B))
     data = x[:1] if B > 1 and x.stride(0) == 0 else x

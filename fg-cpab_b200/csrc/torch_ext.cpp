@@ -65,6 +65,7 @@ class TransformFunction : public torch::autograd::Function<TransformFunction> {
                         std::vector<int64_t> nc, int64_t nstepsolver, bool adaptive,
                         c10::optional<Tensor> order, bool compute_points_grad, bool batched) {
     TORCH_CHECK(points.is_cuda() && theta.is_cuda(), "Only GPU tensors supported");
+    TORCH_CHECK(points.device() == theta.device(), "points and theta must be on one device");
     TORCH_CHECK(points.scalar_type() == at::kFloat && theta.scalar_type() == at::kFloat,
                 "points and theta must be float32");
     const c10::cuda::CUDAGuard guard(theta.device());
@@ -211,8 +212,10 @@ class WarpFunction : public torch::autograd::Function<WarpFunction> {
     std::vector<Tensor> stages(thetas.rbegin(), thetas.rend());  // stage 0 = theta_K
     for (const Tensor &t : stages)
       TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.dim() == 2 &&
-                      t.size(0) == n && t.size(1) == d,
-                  "each theta must be a float32 CUDA tensor [B, ", d, "]");
+                      t.size(0) == n && t.size(1) == d && t.device() == data.device(),
+                  "each theta must be a float32 tensor [B, ", d, "] on x's device");
+    TORCH_CHECK(data.dim() == (int64_t)nc.size() + 2 && (data.size(0) == n || data.size(0) == 1),
+                "x must be [B or 1, C, *spatial] with ", nc.size(), " spatial axes");
     const cpab_stream_t s = stream_of(data);
     Tensor th = K == 1 ? stages[0].contiguous() : at::cat(stages, 0);
     auto tabs = build_tables(B, nd, nC, th, nstepsolver, s);

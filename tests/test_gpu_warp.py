@@ -219,6 +219,8 @@ def test_warp_errors():
         warp(x[:1].clone(), [th], layer.cpab.params)
     with pytest.raises(ValueError):
         warp(x, [th[:, :-1]], layer.cpab.params)
+    with pytest.raises(ValueError):
+        warp(x, [th.cpu()], layer.cpab.params)
     with pytest.raises(AssertionError):
         layer(torch.rand(2, 1, 8, device=DEV), th)
 
