@@ -543,6 +543,61 @@ def phase_ms(rec, steps, world):
             for n in names}
 
 
+E2E_NOTE = ("every step copies its inputs from pinned host memory and its loss and dtheta "
+            "back; the faster of two loops: serial (copy, compute, read-back in sequence, "
+            "CUDA events per step, the 256 MiB L2 flush between steps untimed) and overlapped "
+            "(step j+1's inputs go in on a second stream, after a timed 256 MiB L2 flush on "
+            "that stream, into the other of two input buffers while step j computes; CUDA "
+            "events around the whole loop)")
+
+
+def timed_e2e_overlapped(step, pinned, template, steps, warmup, flush, world, loss_pin,
+                         grad_pin):
+    """ms per step of the end-to-end loop with each step's input copy
+    overlapped with the previous step's compute (double-buffered inputs, copies
+    on a second stream), barrier + synchronize on both sides, max over ranks."""
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    bufs = [{k: torch.empty_like(v) for k, v in template.items()} for _ in range(2)]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def load(b):
+        side.wait_event(done[b])  # the step that last read buffer b has finished
+        with torch.cuda.stream(side):
+            flush.zero_()
+            for k in pinned:
+                bufs[b][k].copy_(pinned[k], non_blocking=True)
+        ready[b].record(side)
+
+    def run(n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(main)
+        side.wait_event(start)
+        load(0)
+        for j in range(n):
+            b = j % 2
+            if j + 1 < n:
+                load(1 - b)
+            main.wait_event(ready[b])
+            loss, grad = step(dict(bufs[b], theta=bufs[b]["theta"].detach()))
+            done[b].record(main)
+            loss_pin.copy_(loss.detach().reshape(1), non_blocking=True)
+            grad_pin.copy_(grad, non_blocking=True)
+        end.record(main)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return start.elapsed_time(end) / n
+
+    run(max(warmup, 1))
+    return max_over_ranks(run(steps), world)
+
+
 def timed_steps(fn, steps, flush, world):
     """ms per step of fn() over `steps` calls: CUDA events per step, L2
     flushed before each (untimed), barrier + synchronize on both sides, max
@@ -833,7 +888,13 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     if clocks is not None:
         clocks.start()
-    e2e_ms = timed_steps(e2e_step, args.steps, flush, world)
+    e2e_serial_ms = timed_steps(e2e_step, args.steps, flush, world)
+    e2e_overlap_ms = timed_e2e_overlapped(step, pinned, resident, args.steps, args.warmup, flush,
+                                          world, loss_pin, grad_pin)
+    # Both loops are ways a user runs the step; the faster one is reported
+    # (overlap wins where the copies are large, the serial loop where the
+    # step is bound by host time and the second stream's bookkeeping adds to it).
+    e2e_ms = min(e2e_serial_ms, e2e_overlap_ms)
     if clocks is not None:
         clocks.pause()
 
@@ -922,7 +983,9 @@ def run_ours(args, rank, world, local):
             "scaling": w.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": cfg,
             "e2e": {"value": pairs_step / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "how": E2E_NOTE, "serial_ms_per_step": e2e_serial_ms,
+                    "overlapped_ms_per_step": e2e_overlap_ms},
             "roofline": {"bound": "hbm",
                          "kernel": "k_backward_mesh (fused resample + adjoint)" if fused
                          else "k_backward_warp (fused grid_sample + adjoint, all stages)"
