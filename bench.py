@@ -547,8 +547,9 @@ E2E_NOTE = ("every step copies its inputs from pinned host memory and its loss a
             "back; the faster of two loops: serial (copy, compute, read-back in sequence, "
             "CUDA events per step, the 256 MiB L2 flush between steps untimed) and overlapped "
             "(step j+1's inputs go in on a second stream, after a timed 256 MiB L2 flush on "
-            "that stream, into the other of two input buffers while step j computes; CUDA "
-            "events around the whole loop)")
+            "that stream, into the other of two input buffers while step j computes, and "
+            "step j's loss and dtheta come back on that stream; CUDA events around the whole "
+            "loop)")
 
 
 def timed_e2e_overlapped(step, pinned, template, steps, warmup, flush, world, loss_pin,
@@ -586,8 +587,16 @@ def timed_e2e_overlapped(step, pinned, template, steps, warmup, flush, world, lo
             main.wait_event(ready[b])
             loss, grad = step(dict(bufs[b], theta=bufs[b]["theta"].detach()))
             done[b].record(main)
-            loss_pin.copy_(loss.detach().reshape(1), non_blocking=True)
-            grad_pin.copy_(grad, non_blocking=True)
+            # the read-back on the second stream too, so that the next step's
+            # launches do not wait for it
+            side.wait_event(done[b])
+            loss, grad = loss.detach(), grad.detach()
+            loss.record_stream(side)
+            grad.record_stream(side)
+            with torch.cuda.stream(side):
+                loss_pin.copy_(loss.reshape(1), non_blocking=True)
+                grad_pin.copy_(grad, non_blocking=True)
+        main.wait_stream(side)
         end.record(main)
         torch.cuda.synchronize()
         if world > 1:
